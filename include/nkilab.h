@@ -1,0 +1,142 @@
+/*
+ * nkilab.h - C ABI of the B200 (sm_100a) kernel set behind nkilab.ops.
+ *
+ * Every entry point takes caller-owned DEVICE pointers, plain integer sizes and a
+ * cudaStream_t passed as `void*` (NULL = legacy default stream). Nothing here
+ * allocates device memory, synchronises the stream or aborts: each call validates
+ * its arguments on the host, enqueues its kernels asynchronously and returns an
+ * nkl_status. nkl_last_error() gives a human-readable message for the most recent
+ * failing call on the calling thread. No call keeps mutable global state on the
+ * host, so calls are thread-safe as long as callers do not share output buffers.
+ *
+ * Layouts are row-major and dense (the innermost dimension is contiguous):
+ *   row kernels  x, y      [rows, cols]
+ *   matmul       a [M, K], b [K, N], c [M, N]
+ *   attention    q, k, v, out [heads, seq, head_dim]
+ *
+ * dtype is NKL_FLOAT32 or NKL_BFLOAT16 and applies to every tensor argument of a
+ * call (inputs and output share one dtype, as in the reference, where each kernel
+ * allocates its output with the input's dtype).
+ *
+ * Each declaration cites the reference interface it replaces, as path:line within
+ * Nags-gk/nki-kernel-lab. In the reference each op is a Python function that pads /
+ * transposes NumPy arrays and runs an NKI kernel on the CPU simulator; here the
+ * same op is one C call over device memory.
+ */
+#ifndef NKILAB_H_
+#define NKILAB_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NKL_ABI_VERSION 1
+
+typedef enum nkl_status {
+  NKL_OK = 0,
+  NKL_ERR_SHAPE = 1,      /* a size is out of the supported range (reference: kernel assert) */
+  NKL_ERR_DTYPE = 2,      /* dtype is not NKL_FLOAT32 / NKL_BFLOAT16, or unsupported for the op */
+  NKL_ERR_ALIGN = 3,      /* a pointer is not aligned as the op requires (see each op) */
+  NKL_ERR_CUDA = 4,       /* a CUDA runtime / driver call or kernel launch failed */
+  NKL_ERR_ARG = 5,        /* NULL pointer, too-small workspace, bad flag */
+  NKL_ERR_DEVICE = 7      /* a kernel reported a device-side failure (bounded wait expired) */
+} nkl_status;
+
+typedef enum nkl_dtype { NKL_FLOAT32 = 0, NKL_BFLOAT16 = 1 } nkl_dtype;
+
+/* ---- library ------------------------------------------------------------------ */
+
+/* ABI version (NKL_ABI_VERSION). No reference counterpart: nkilab/__init__.py:12
+ * carries only a Python __version__. */
+int nkl_abi_version(void);
+
+/* Static string for a status code. */
+const char* nkl_status_string(int status);
+
+/* Message of the most recent failing call on this host thread ("" if none). */
+const char* nkl_last_error(void);
+
+/* Device-side failure flag: kernels that wait on hardware barriers give up after a
+ * bounded number of polls, set this flag and return early. This call synchronises
+ * `stream`, reads the flag of the current device, clears it and returns NKL_OK or
+ * NKL_ERR_DEVICE. The reference has no device and no counterpart. */
+int nkl_check_device(void* stream);
+
+/* ---- row kernels (nkilab/kernels/norm.py) ------------------------------------- */
+
+/* y = x * rsqrt(mean(x^2) + eps) * weight, fp32 statistics, one HBM pass.
+ * x, out [rows, cols]; weight [cols].
+ * Replaces nkilab/ops.py:60-61 (rmsnorm) -> nkilab/kernels/norm.py:92-118 (rmsnorm_fused). */
+int nkl_rmsnorm(const void* x, const void* weight, void* out, int64_t rows, int64_t cols,
+                float eps, int dtype, void* stream);
+
+/* Row softmax over the last dim, one HBM pass: y = exp(x - max) * (1 / sum).
+ * Replaces nkilab/ops.py:55-57 (softmax, fused=True) -> nkilab/kernels/norm.py:65-89. */
+int nkl_softmax(const void* x, void* out, int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* Bytes of device workspace nkl_softmax_unfused needs for a [rows, cols] input. */
+size_t nkl_softmax_unfused_workspace_size(int64_t rows, int64_t cols);
+
+/* Three-pass softmax that round-trips its intermediates through HBM: row max, then
+ * e = exp(x - max) (fp32) with row sums, then y = e / sum. Workspace is caller-owned,
+ * at least nkl_softmax_unfused_workspace_size() bytes, 256-byte aligned.
+ * Replaces nkilab/ops.py:55-57 (softmax, fused=False) -> nkilab/kernels/norm.py:22-62. */
+int nkl_softmax_unfused(const void* x, void* out, void* workspace, size_t workspace_bytes,
+                        int64_t rows, int64_t cols, int dtype, void* stream);
+
+/* y = silu(gate) * up, elementwise over [rows, cols], fp32 silu.
+ * Replaces nkilab/ops.py:64-65 (swiglu) -> nkilab/kernels/norm.py:121-136 (swiglu_fused). */
+int nkl_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+               int dtype, void* stream);
+
+/* ---- GEMM (nkilab/kernels/matmul.py) ------------------------------------------ */
+
+/* c[M,N] = a[M,K] @ b[K,N], fp32 accumulation, one rounding to dtype on the way out.
+ * bf16: TMA + tcgen05 tensor cores (accumulator in TMEM); requires K and N to be
+ * multiples of 8 (16-byte rows for TMA) and 16-byte aligned pointers.
+ * fp32: exact fp32 FMA path (no TF32), any shape.
+ * Replaces nkilab/ops.py:38-52 (matmul, variant="blocked")
+ *   -> nkilab/kernels/matmul.py:46-82 (matmul_blocked). */
+int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
+               int dtype, void* stream);
+
+/* Same product computed the way the reference's naive kernel does it: no operand
+ * reuse, every (m, n, k) step reloads both tiles from global memory (plain CUDA
+ * cores, fp32 accumulation). Kept as the unblocked rung of the ladder.
+ * Replaces nkilab/ops.py:47-48 (matmul, variant="naive")
+ *   -> nkilab/kernels/matmul.py:24-43 (matmul_naive). */
+int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
+                     int dtype, void* stream);
+
+/* ---- causal attention (nkilab/kernels/attention.py) --------------------------- */
+
+/* out = softmax(q k^T * scale + causal mask) v per head, fp32 softmax statistics,
+ * P rounded to dtype before the P.V product, output rounded once.
+ * bf16: tcgen05 flash kernel (TMA-staged tiles, S and P.V accumulators in TMEM,
+ * online softmax, fully masked key tiles skipped); head_dim 64 or 128, any seq.
+ * fp32: exact fp32 flash kernel on CUDA cores; head_dim <= 128, any seq.
+ * Replaces nkilab/ops.py:77-91 (attention, any "flash*" variant)
+ *   -> nkilab/kernels/attention.py:155-325. */
+int nkl_attention(const void* q, const void* k, const void* v, void* out, int64_t heads,
+                  int64_t seq, int64_t head_dim, float scale, int dtype, void* stream);
+
+/* Bytes of device workspace nkl_attention_naive needs: fp32 scores and dtype
+ * probabilities, each [heads, seq, seq]. */
+size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype);
+
+/* Unfused attention that materialises the masked score matrix (fp32) and the
+ * normalised probabilities (dtype) in HBM, then multiplies by v.
+ * Replaces nkilab/ops.py:77-91 (attention, variant="naive")
+ *   -> nkilab/kernels/attention.py:35-89 (attention_naive). */
+int nkl_attention_naive(const void* q, const void* k, const void* v, void* out,
+                        void* workspace, size_t workspace_bytes, int64_t heads, int64_t seq,
+                        int64_t head_dim, float scale, int dtype, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* NKILAB_H_ */

@@ -1,0 +1,53 @@
+// capi.cu - library-level C entry points: version, status strings, the per-thread
+// error message and the device-failure check. The op entry points live beside their
+// kernels (rows.cu, gemm.cu, attention.cu).
+#include "common.cuh"
+
+namespace nkl {
+
+char* last_error_buffer() {
+  static thread_local char buf[512] = {0};
+  return buf;
+}
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+}  // namespace nkl
+
+extern "C" int nkl_abi_version(void) { return NKL_ABI_VERSION; }
+
+extern "C" const char* nkl_status_string(int status) {
+  switch (status) {
+    case NKL_OK: return "ok";
+    case NKL_ERR_SHAPE: return "unsupported shape";
+    case NKL_ERR_DTYPE: return "unsupported dtype";
+    case NKL_ERR_ALIGN: return "misaligned pointer";
+    case NKL_ERR_CUDA: return "CUDA error";
+    case NKL_ERR_ARG: return "invalid argument";
+    case NKL_ERR_DEVICE: return "device-side failure (bounded wait expired)";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* nkl_last_error(void) { return nkl::last_error_buffer(); }
+
+extern "C" int nkl_check_device(void* stream) {
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return nkl::fail(NKL_ERR_CUDA, "nkl_check_device: %s", cudaGetErrorString(e));
+  const int g = nkl::gemm_read_and_clear_device_error();
+  const int a = nkl::attention_read_and_clear_device_error();
+  if (g < 0 || a < 0) return nkl::fail(NKL_ERR_CUDA, "nkl_check_device: could not read the device flag");
+  if (g || a)
+    return nkl::fail(NKL_ERR_DEVICE, "nkl_check_device: kernel gave up waiting (gemm code %d, attention code %d)", g, a);
+  return NKL_OK;
+}

@@ -1,0 +1,431 @@
+// rows.cu - memory-bound row kernels: RMSNorm, softmax (fused and unfused), SwiGLU.
+//
+// Reference algorithms (Nags-gk/nki-kernel-lab):
+//   rmsnorm_fused    nkilab/kernels/norm.py:92-118
+//   softmax_fused    nkilab/kernels/norm.py:65-89
+//   softmax_unfused  nkilab/kernels/norm.py:22-62
+//   swiglu_fused     nkilab/kernels/norm.py:121-136
+// The reference tiles 128 rows onto SBUF partitions; on B200 a row maps to one warp
+// (rows up to 512 16-byte vectors) held entirely in registers, so every byte of the
+// input is read from HBM once and every output byte written once, with 16-byte
+// coalesced accesses. Rows that are too long or not 16-byte aligned fall back to a
+// block-per-row kernel that streams the row more than once (still exact).
+//
+// Rounding points follow the reference: statistics in fp32, one rounding to the
+// output dtype at the end (rmsnorm rounds x*rstd to fp32 before the weight multiply,
+// norm.py:114-116; fused softmax multiplies by a reciprocal, norm.py:84-87; unfused
+// softmax divides, norm.py:142).
+#include "common.cuh"
+
+namespace nkl {
+namespace {
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kMaxVecPerLane = 16;  // 512 vectors per row: 4096 bf16 / 2048 fp32 columns
+
+// ------------------------------------------------------------------ RMSNorm
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                    int64_t rows, int cols, float inv_cols, float eps) {
+  constexpr int V = Vec16<T>::N;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = cols / V;
+  const T* xr = x + row * cols;
+  T* yr = y + row * cols;
+
+  Vec16<T> xv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) xv[i].raw = ld_stream(xr + (int64_t)j * V);
+    else xv[i].raw = make_uint4(0u, 0u, 0u, 0u);
+  }
+  float ssq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+#pragma unroll
+    for (int e = 0; e < V; ++e) { const float f = xv[i].get(e); ssq += f * f; }
+  }
+  ssq = warp_sum(ssq);
+  const float rstd = rsqrtf(ssq * inv_cols + eps);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) {
+      Vec16<T> wv;
+      wv.raw = *reinterpret_cast<const uint4*>(w + (int64_t)j * V);
+      float o[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        const float xn = xv[i].get(e) * rstd;  // fp32 x * rstd, then * weight
+        o[e] = xn * wv.get(e);
+      }
+      st_stream(yr + (int64_t)j * V, pack16<T>(o));
+    }
+  }
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < nw) ? red[l] : 0.f;
+  return warp_sum(t);
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = (l < nw) ? red[l] : -INFINITY;
+  return warp_max(t);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+rmsnorm_block_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
+                     int64_t rows, int64_t cols, float inv_cols, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  T* yr = y + row * cols;
+  float ssq = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) { const float f = to_f32(xr[c]); ssq += f * f; }
+  ssq = block_sum(ssq, red);
+  const float rstd = rsqrtf(ssq * inv_cols + eps);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float xn = to_f32(xr[c]) * rstd;
+    yr[c] = from_f32<T>(xn * to_f32(w[c]));
+  }
+}
+
+// ------------------------------------------------------------------ fused softmax
+
+template <typename T, int NV>
+__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols) {
+  constexpr int V = Vec16<T>::N;
+  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = cols / V;
+  const T* xr = x + row * cols;
+  T* yr = y + row * cols;
+
+  Vec16<T> xv[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) xv[i].raw = ld_stream(xr + (int64_t)j * V);
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i * 32 + lane < nvec) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) m = fmaxf(m, xv[i].get(e));
+    }
+  }
+  const float neg_max = -warp_max(m);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    if (i * 32 + lane < nvec) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) s += row_exp<T>(xv[i].get(e) + neg_max);
+    }
+  }
+  const float rinv = 1.0f / warp_sum(s);
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) {
+      float o[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = row_exp<T>(xv[i].get(e) + neg_max) * rinv;
+      st_stream(yr + (int64_t)j * V, pack16<T>(o));
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+softmax_block_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int64_t cols) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  T* yr = y + row * cols;
+  float m = -INFINITY;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, to_f32(xr[c]));
+  const float neg_max = -block_max(m, red);
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) s += row_exp<T>(to_f32(xr[c]) + neg_max);
+  const float rinv = 1.0f / block_sum(s, red);
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x)
+    yr[c] = from_f32<T>(row_exp<T>(to_f32(xr[c]) + neg_max) * rinv);
+}
+
+// ------------------------------------------------------------------ unfused softmax
+// Three launches, each a full HBM round trip, as in norm.py:22-62:
+//   pass 1  m[r] = max_c x[r,c]                        -> workspace
+//   pass 2  e[r,c] = exp(x[r,c] - m[r]) (fp32), s[r] = sum_c e[r,c]  -> workspace
+//   pass 3  y[r,c] = e[r,c] / s[r]
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+softmax_pass_max(const T* __restrict__ x, float* __restrict__ m_out, int64_t cols) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  float m = -INFINITY;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) m = fmaxf(m, to_f32(xr[c]));
+  m = block_max(m, red);
+  if (threadIdx.x == 0) m_out[row] = m;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+softmax_pass_exp(const T* __restrict__ x, const float* __restrict__ m_in, float* __restrict__ e_out,
+                 float* __restrict__ s_out, int64_t cols) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * cols;
+  float* er = e_out + row * cols;
+  const float m = m_in[row];
+  float s = 0.f;
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) {
+    const float sh = to_f32(xr[c]) - m;
+    const float e = row_exp<float>(sh);
+    er[c] = e;
+    s += e;
+  }
+  s = block_sum(s, red);
+  if (threadIdx.x == 0) s_out[row] = s;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+softmax_pass_div(const float* __restrict__ e_in, const float* __restrict__ s_in, T* __restrict__ y,
+                 int64_t cols) {
+  const int64_t row = blockIdx.x;
+  const float* er = e_in + row * cols;
+  T* yr = y + row * cols;
+  const float s = s_in[row];
+  for (int64_t c = threadIdx.x; c < cols; c += blockDim.x) yr[c] = from_f32<T>(er[c] / s);
+}
+
+// ------------------------------------------------------------------ SwiGLU
+
+template <typename T>
+__device__ __forceinline__ float silu_f32(float g) {
+  if constexpr (sizeof(T) == 4) return g / (1.0f + expf(-g));
+  else return __fdividef(g, 1.0f + __expf(-g));
+}
+
+constexpr int kSwigluThreads = 256;
+constexpr int kSwigluUnroll = 4;
+
+// Every thread handles kSwigluUnroll 16-byte vectors of gate and up, all loads
+// issued before any math so 8 x 16 B are in flight per thread.
+template <typename T>
+__global__ void __launch_bounds__(kSwigluThreads)
+swiglu_vec_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t nvec) {
+  constexpr int V = Vec16<T>::N;
+  const int64_t base = (int64_t)blockIdx.x * kSwigluThreads * kSwigluUnroll + threadIdx.x;
+  Vec16<T> gv[kSwigluUnroll], uv[kSwigluUnroll];
+#pragma unroll
+  for (int i = 0; i < kSwigluUnroll; ++i) {
+    const int64_t j = base + (int64_t)i * kSwigluThreads;
+    if (j < nvec) {
+      gv[i].raw = ld_stream(g + j * V);
+      uv[i].raw = ld_stream(u + j * V);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kSwigluUnroll; ++i) {
+    const int64_t j = base + (int64_t)i * kSwigluThreads;
+    if (j < nvec) {
+      float o[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = silu_f32<T>(gv[i].get(e)) * uv[i].get(e);
+      st_stream(y + j * V, pack16<T>(o));
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+swiglu_scalar_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    y[i] = from_f32<T>(silu_f32<T>(to_f32(g[i])) * to_f32(u[i]));
+}
+
+// ------------------------------------------------------------------ dispatch
+
+template <typename T>
+bool row_vectorizable(int64_t cols, const void* a, const void* b, const void* c) {
+  constexpr int V = 16 / sizeof(T);
+  return cols % V == 0 && cols / V <= 32 * kMaxVecPerLane && is_aligned(a, 16) && is_aligned(b, 16) &&
+         (c == nullptr || is_aligned(c, 16));
+}
+
+// Vectors per lane rounded up to a power of two (1..16).
+inline int nv_bucket(int64_t nvec) {
+  const int64_t per_lane = (nvec + 31) / 32;
+  int nv = 1;
+  while (nv < per_lane) nv <<= 1;
+  return nv;
+}
+
+template <typename T>
+int rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int64_t cols, float eps,
+                   cudaStream_t st) {
+  const float inv_cols = (float)(1.0 / (double)cols);
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(w);
+  T* yp = static_cast<T*>(y);
+  if (row_vectorizable<T>(cols, x, y, w)) {
+    const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
+    const unsigned grid = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
+    const int c = (int)cols;
+    switch (nv) {
+      case 1: rmsnorm_warp_kernel<T, 1><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+      case 2: rmsnorm_warp_kernel<T, 2><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+      case 4: rmsnorm_warp_kernel<T, 4><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+      case 8: rmsnorm_warp_kernel<T, 8><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+      default: rmsnorm_warp_kernel<T, 16><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+    }
+  } else {
+    rmsnorm_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, wp, yp, rows, cols, inv_cols, eps);
+  }
+  return check_launch("nkl_rmsnorm");
+}
+
+template <typename T>
+int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStream_t st) {
+  const T* xp = static_cast<const T*>(x);
+  T* yp = static_cast<T*>(y);
+  if (row_vectorizable<T>(cols, x, y, nullptr)) {
+    const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
+    const unsigned grid = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
+    const int c = (int)cols;
+    switch (nv) {
+      case 1: softmax_warp_kernel<T, 1><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+      case 2: softmax_warp_kernel<T, 2><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+      case 4: softmax_warp_kernel<T, 4><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+      case 8: softmax_warp_kernel<T, 8><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+      default: softmax_warp_kernel<T, 16><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+    }
+  } else {
+    softmax_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, yp, rows, cols);
+  }
+  return check_launch("nkl_softmax");
+}
+
+// Workspace layout of the unfused softmax: m [rows] | s [rows] | e [rows, cols], each
+// fp32 and each region starting on a 256-byte boundary.
+inline size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+
+template <typename T>
+int softmax_unfused_launch(const void* x, void* y, void* ws, int64_t rows, int64_t cols, cudaStream_t st) {
+  float* m = static_cast<float*>(ws);
+  float* s = reinterpret_cast<float*>(static_cast<char*>(ws) + round256(rows * sizeof(float)));
+  float* e = reinterpret_cast<float*>(static_cast<char*>(ws) + 2 * round256(rows * sizeof(float)));
+  const T* xp = static_cast<const T*>(x);
+  softmax_pass_max<T><<<(unsigned)rows, 256, 0, st>>>(xp, m, cols);
+  softmax_pass_exp<T><<<(unsigned)rows, 256, 0, st>>>(xp, m, e, s, cols);
+  softmax_pass_div<T><<<(unsigned)rows, 256, 0, st>>>(e, s, static_cast<T*>(y), cols);
+  return check_launch("nkl_softmax_unfused");
+}
+
+template <typename T>
+int swiglu_launch(const void* g, const void* u, void* y, int64_t n, cudaStream_t st) {
+  constexpr int V = 16 / sizeof(T);
+  const T* gp = static_cast<const T*>(g);
+  const T* up = static_cast<const T*>(u);
+  T* yp = static_cast<T*>(y);
+  if (n % V == 0 && is_aligned(g, 16) && is_aligned(u, 16) && is_aligned(y, 16)) {
+    const int64_t nvec = n / V;
+    const int64_t per_block = (int64_t)kSwigluThreads * kSwigluUnroll;
+    const unsigned grid = (unsigned)((nvec + per_block - 1) / per_block);
+    swiglu_vec_kernel<T><<<grid, kSwigluThreads, 0, st>>>(gp, up, yp, nvec);
+  } else {
+    int64_t blocks = (n + 255) / 256;
+    const int64_t cap = (int64_t)sm_count() * 8;
+    if (blocks > cap) blocks = cap;
+    swiglu_scalar_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(gp, up, yp, n);
+  }
+  return check_launch("nkl_swiglu");
+}
+
+int check_rows(const char* op, int64_t rows, int64_t cols, int dtype) {
+  if (!valid_dtype(dtype)) return fail(NKL_ERR_DTYPE, "%s: unsupported dtype %d", op, dtype);
+  if (rows < 0 || cols < 1) return fail(NKL_ERR_SHAPE, "%s: bad shape [%lld, %lld]", op, (long long)rows, (long long)cols);
+  if (rows > 0x7fffffffLL) return fail(NKL_ERR_SHAPE, "%s: rows %lld exceed 2^31-1", op, (long long)rows);
+  return NKL_OK;
+}
+
+}  // namespace
+}  // namespace nkl
+
+using namespace nkl;
+
+extern "C" int nkl_rmsnorm(const void* x, const void* weight, void* out, int64_t rows, int64_t cols,
+                           float eps, int dtype, void* stream) {
+  int rc = check_rows("nkl_rmsnorm", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!x || !weight || !out) return fail(NKL_ERR_ARG, "nkl_rmsnorm: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NKL_FLOAT32 ? rmsnorm_launch<float>(x, weight, out, rows, cols, eps, st)
+                              : rmsnorm_launch<bf16>(x, weight, out, rows, cols, eps, st);
+}
+
+extern "C" int nkl_softmax(const void* x, void* out, int64_t rows, int64_t cols, int dtype, void* stream) {
+  int rc = check_rows("nkl_softmax", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!x || !out) return fail(NKL_ERR_ARG, "nkl_softmax: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NKL_FLOAT32 ? softmax_launch<float>(x, out, rows, cols, st)
+                              : softmax_launch<bf16>(x, out, rows, cols, st);
+}
+
+extern "C" size_t nkl_softmax_unfused_workspace_size(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return 2 * round256((size_t)rows * sizeof(float)) + round256((size_t)rows * (size_t)cols * sizeof(float));
+}
+
+extern "C" int nkl_softmax_unfused(const void* x, void* out, void* workspace, size_t workspace_bytes,
+                                   int64_t rows, int64_t cols, int dtype, void* stream) {
+  int rc = check_rows("nkl_softmax_unfused", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!x || !out || !workspace) return fail(NKL_ERR_ARG, "nkl_softmax_unfused: NULL pointer");
+  if (workspace_bytes < nkl_softmax_unfused_workspace_size(rows, cols))
+    return fail(NKL_ERR_ARG, "nkl_softmax_unfused: workspace %zu B < required %zu B", workspace_bytes,
+                nkl_softmax_unfused_workspace_size(rows, cols));
+  if (!is_aligned(workspace, 256)) return fail(NKL_ERR_ALIGN, "nkl_softmax_unfused: workspace not 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NKL_FLOAT32 ? softmax_unfused_launch<float>(x, out, workspace, rows, cols, st)
+                              : softmax_unfused_launch<bf16>(x, out, workspace, rows, cols, st);
+}
+
+extern "C" int nkl_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,
+                          int dtype, void* stream) {
+  int rc = check_rows("nkl_swiglu", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!gate || !up || !out) return fail(NKL_ERR_ARG, "nkl_swiglu: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NKL_FLOAT32 ? swiglu_launch<float>(gate, up, out, rows * cols, st)
+                              : swiglu_launch<bf16>(gate, up, out, rows * cols, st);
+}

@@ -1,0 +1,144 @@
+"""PyTorch custom ops (namespace ``nkilab``) over the C ABI.
+
+Each op takes contiguous CUDA tensors, allocates its output with the caching
+allocator, and launches the C-ABI entry point on the current CUDA stream, so the ops
+compose with streams and CUDA-graph capture like any torch op:
+
+    torch.ops.nkilab.rmsnorm(x, weight, eps)        -> nkl_rmsnorm
+    torch.ops.nkilab.softmax(x, fused)              -> nkl_softmax / nkl_softmax_unfused
+    torch.ops.nkilab.swiglu(gate, up)               -> nkl_swiglu
+    torch.ops.nkilab.matmul(a, b, naive)            -> nkl_matmul / nkl_matmul_naive
+    torch.ops.nkilab.attention(q, k, v, scale, naive) -> nkl_attention / nkl_attention_naive
+
+There is no CPU implementation: a CPU tensor is an error, never a fallback.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+_DTYPES = {torch.float32: N.FLOAT32, torch.bfloat16: N.BFLOAT16}
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise TypeError(f"nkilab kernels support float32 and bfloat16, got {t.dtype}") from None
+
+
+def _prep(*ts: torch.Tensor):
+    dev = ts[0].device
+    if dev.type != "cuda":
+        raise RuntimeError("nkilab ops run on CUDA tensors only (no CPU implementation)")
+    for t in ts:
+        if t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {t.device} vs {dev}")
+        if t.dtype != ts[0].dtype:
+            raise TypeError(f"mixed dtypes: {t.dtype} vs {ts[0].dtype}")
+        if not t.is_contiguous():
+            raise RuntimeError("nkilab ops need contiguous tensors")
+    return dev, dtype_code(ts[0]), torch.cuda.current_stream(dev).cuda_stream
+
+
+def _rows(x: torch.Tensor):
+    cols = x.shape[-1] if x.dim() else 1
+    rows = x.numel() // cols if cols else 0
+    return rows, cols
+
+
+@torch.library.custom_op("nkilab::rmsnorm", mutates_args=())
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    dev, dt, st = _prep(x, weight)
+    rows, cols = _rows(x)
+    if weight.numel() != cols:
+        raise ValueError(f"weight has {weight.numel()} elements, rows have {cols}")
+    out = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        N.call("nkl_rmsnorm", x.data_ptr(), weight.data_ptr(), out.data_ptr(), rows, cols, eps, dt, st)
+    return out
+
+
+@rmsnorm.register_fake
+def _(x, weight, eps):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("nkilab::softmax", mutates_args=())
+def softmax(x: torch.Tensor, fused: bool) -> torch.Tensor:
+    dev, dt, st = _prep(x)
+    rows, cols = _rows(x)
+    out = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        if fused:
+            N.call("nkl_softmax", x.data_ptr(), out.data_ptr(), rows, cols, dt, st)
+        else:
+            nbytes = N.lib.nkl_softmax_unfused_workspace_size(rows, cols)
+            ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+            N.call("nkl_softmax_unfused", x.data_ptr(), out.data_ptr(), ws.data_ptr(), nbytes, rows, cols, dt, st)
+    return out
+
+
+@softmax.register_fake
+def _(x, fused):
+    return torch.empty_like(x)
+
+
+@torch.library.custom_op("nkilab::swiglu", mutates_args=())
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    dev, dt, st = _prep(gate, up)
+    if gate.shape != up.shape:
+        raise ValueError(f"gate {tuple(gate.shape)} and up {tuple(up.shape)} differ")
+    rows, cols = _rows(gate)
+    out = torch.empty_like(gate)
+    with torch.cuda.device(dev):
+        N.call("nkl_swiglu", gate.data_ptr(), up.data_ptr(), out.data_ptr(), rows, cols, dt, st)
+    return out
+
+
+@swiglu.register_fake
+def _(gate, up):
+    return torch.empty_like(gate)
+
+
+@torch.library.custom_op("nkilab::matmul", mutates_args=())
+def matmul(a: torch.Tensor, b: torch.Tensor, naive: bool) -> torch.Tensor:
+    dev, dt, st = _prep(a, b)
+    M, K = a.shape
+    K2, Ncols = b.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {tuple(a.shape)} @ {tuple(b.shape)}")
+    out = torch.empty((M, Ncols), dtype=a.dtype, device=dev)
+    with torch.cuda.device(dev):
+        fn = "nkl_matmul_naive" if naive else "nkl_matmul"
+        N.call(fn, a.data_ptr(), b.data_ptr(), out.data_ptr(), M, Ncols, K, dt, st)
+    return out
+
+
+@matmul.register_fake
+def _(a, b, naive):
+    return a.new_empty((a.shape[0], b.shape[1]))
+
+
+@torch.library.custom_op("nkilab::attention", mutates_args=())
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, naive: bool) -> torch.Tensor:
+    dev, dt, st = _prep(q, k, v)
+    H, S, d = q.shape
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must match")
+    out = torch.empty_like(q)
+    with torch.cuda.device(dev):
+        if naive:
+            nbytes = N.lib.nkl_attention_naive_workspace_size(H, S, dt)
+            ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+            N.call("nkl_attention_naive", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                   nbytes, H, S, d, scale, dt, st)
+        else:
+            N.call("nkl_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, S, d, scale, dt, st)
+    return out
+
+
+@attention.register_fake
+def _(q, k, v, scale, naive):
+    return torch.empty_like(q)

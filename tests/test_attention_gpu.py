@@ -1,0 +1,133 @@
+"""GPU parity of causal attention (tcgen05 flash bf16, exact fp32 flash, naive)."""
+from __future__ import annotations
+
+import ml_dtypes
+import numpy as np
+import pytest
+import torch
+
+from conftest import bf16_ulp_diff, cases, load_golden, rel_err, to_numpy, to_torch
+from oracle import nki_oracle as O
+
+pytestmark = pytest.mark.gpu
+BF16 = ml_dtypes.bfloat16
+ATT = load_golden("golden_attention.npz")
+FLASH = ["flash", "flash_kv_resident", "flash_balanced", "flash_pipelined"]
+
+
+@pytest.fixture(scope="module")
+def ops():
+    from nkilab import ops as _ops
+
+    return _ops
+
+
+def _sdpa(q, k, v):
+    return torch.nn.functional.scaled_dot_product_attention(*map(torch.from_numpy, (q, k, v)), is_causal=True).numpy()
+
+
+@pytest.mark.parametrize("case", cases(ATT))
+def test_attention_matches_reference_golden(ops, case):
+    q, k, v = (ATT[f"{case}/{n}"] for n in "qkv")
+    for key in [k_ for k_ in ATT if k_.startswith(case + "/out_")]:
+        variant = key.split("/out_")[1]
+        out = ops.attention(q, k, v, variant=variant)
+        gold = ATT[key]
+        assert out.shape == gold.shape and out.dtype == gold.dtype
+        if gold.dtype == BF16:
+            assert rel_err(out.astype(np.float32), gold.astype(np.float32)) < 3e-3, variant
+        else:
+            np.testing.assert_allclose(out, gold, atol=2e-5)
+
+
+@pytest.mark.parametrize("variant", ["naive"] + FLASH)
+@pytest.mark.parametrize("H,S,d", [(1, 128, 64), (2, 512, 64), (2, 200, 32), (1, 384, 128)])
+def test_attention_matches_torch_fp32(ops, rng, variant, H, S, d):
+    q, k, v = (rng.standard_normal((H, S, d)).astype(np.float32) for _ in range(3))
+    out = ops.attention(q, k, v, variant=variant)
+    assert out.shape == (H, S, d)
+    np.testing.assert_allclose(out, _sdpa(q, k, v), atol=2e-5)
+
+
+@pytest.mark.parametrize("variant", ["naive", "flash_pipelined"])
+def test_attention_bf16(ops, rng, variant):
+    q, k, v = (rng.standard_normal((2, 256, 64)).astype(BF16) for _ in range(3))
+    ref = _sdpa(*(t.astype(np.float32) for t in (q, k, v)))
+    assert rel_err(ops.attention(q, k, v, variant=variant).astype(np.float32), ref) < 3e-2
+
+
+def test_first_token_attends_only_to_itself(ops, rng):
+    q, k, v = (rng.standard_normal((1, 256, 64)).astype(np.float32) for _ in range(3))
+    out = ops.attention(q, k, v)
+    np.testing.assert_allclose(out[0, 0], v[0, 0], atol=1e-6)
+
+
+@pytest.mark.parametrize("dtype", [np.float32, BF16])
+def test_variants_agree_bitwise_on_flash_family(ops, rng, dtype):
+    q, k, v = (rng.standard_normal((2, 512, 64)).astype(dtype) for _ in range(3))
+    outs = [ops.attention(q, k, v, variant=n) for n in ("flash_balanced", "flash_pipelined")]
+    np.testing.assert_array_equal(outs[0].view(np.uint8), outs[1].view(np.uint8))
+
+
+def _check_vs_oracle(out_dev, q, k, v, rel=3e-3):
+    ref = O.attention_flash(q, k, v)
+    got = out_dev.float().cpu().numpy()
+    assert rel_err(got, ref.float().numpy()) < rel
+
+
+@pytest.mark.parametrize("H,S", [(8, 2048), (1, 4096)])
+def test_attention_baseline_configs(ops, H, S):
+    """causal 8 x 2048 x 128 and 1 x 4096 x 128 bf16 vs the oracle."""
+    g = torch.Generator().manual_seed(H * 10000 + S)
+    q, k, v = (torch.randn(H, S, 128, generator=g).to(torch.bfloat16) for _ in range(3))
+    out = ops.attention(q.cuda(), k.cuda(), v.cuda())
+    _check_vs_oracle(out, q, k, v)
+
+
+@pytest.mark.parametrize("H,S,d", [(1, 1, 128), (3, 129, 64), (2, 200, 128), (1, 257, 64), (2, 130, 32),
+                                   (1, 640, 96), (4, 1000, 128)])
+def test_attention_bf16_edge_shapes(ops, H, S, d):
+    g = torch.Generator().manual_seed(H * 7 + S * 3 + d)
+    q, k, v = (torch.randn(H, S, d, generator=g).to(torch.bfloat16) for _ in range(3))
+    out = ops.attention(q.cuda(), k.cuda(), v.cuda())
+    assert out.shape == (H, S, d)
+    _check_vs_oracle(out, q, k, v)
+
+
+def test_attention_is_causal(ops):
+    """Changing keys/values after position t leaves outputs up to t unchanged (bitwise)."""
+    g = torch.Generator().manual_seed(11)
+    q, k, v = (torch.randn(2, 1024, 128, generator=g).to(torch.bfloat16).cuda() for _ in range(3))
+    out1 = ops.attention(q, k, v)
+    k2, v2 = k.clone(), v.clone()
+    k2[:, 600:] = torch.randn_like(k2[:, 600:].float()).to(torch.bfloat16)
+    v2[:, 600:] = 7.0
+    out2 = ops.attention(q, k2, v2)
+    assert torch.equal(out1[:, :600], out2[:, :600])
+    assert not torch.equal(out1[:, 600:], out2[:, 600:])
+
+
+def test_attention_rows_are_convex_combinations(ops):
+    """With v = const c in one column, that output column equals c (softmax rows sum to 1)."""
+    g = torch.Generator().manual_seed(12)
+    q, k = (torch.randn(4, 2048, 128, generator=g).to(torch.bfloat16).cuda() for _ in range(2))
+    v = torch.randn(4, 2048, 128, generator=g).to(torch.bfloat16).cuda()
+    v[..., 5] = 0.5
+    out = ops.attention(q, k, v)
+    np.testing.assert_allclose(out[..., 5].float().cpu().numpy(), 0.5, atol=4e-3)
+
+
+def test_kernel_level_layout(rng):
+    """The reference's kernel-level layout: qT, kT [H, d, S], v [H, S, d]."""
+    from nkilab.kernels import attention as at
+
+    q, k, v = (rng.standard_normal((2, 256, 64)).astype(np.float32) for _ in range(3))
+    qT, kT = (np.ascontiguousarray(t.transpose(0, 2, 1)) for t in (q, k))
+    for fn in (at.attention_naive, at.flash_attention, at.flash_attention_pipelined):
+        np.testing.assert_allclose(fn(qT, kT, v, 1 / 8.0), _sdpa(q, k, v), atol=2e-5)
+
+
+def test_device_flag_clean_after_runs():
+    from nkilab import _native as N
+
+    N.check_device(torch.cuda.current_stream().cuda_stream)

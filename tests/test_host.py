@@ -1,0 +1,95 @@
+"""Host-side logic of the drop-in boundary that needs no GPU (CPU only)."""
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN
+
+
+def test_choose_blocks_respects_psum_banks():
+    """tests/test_matmul.py:40-45 of the reference."""
+    from nkilab import ops
+
+    for mt in range(1, 9):
+        for nt in range(1, 17):
+            bm, bn = ops.choose_blocks(mt, nt)
+            assert bm * bn <= 8 and mt % bm == 0 and nt % bn == 0
+    assert ops.choose_blocks(4, 4) in {(2, 4), (4, 2)}
+
+
+def test_choose_blocks_matches_reference_table():
+    from nkilab import ops
+
+    with open(os.path.join(GOLDEN, "golden_blocks.json")) as f:
+        table = json.load(f)
+    for key, want in table.items():
+        m, n = map(int, key.split(","))
+        assert list(ops.choose_blocks(m, n)) == want
+
+
+def test_blocked_rejects_psum_overflow():
+    """tests/test_matmul.py:33-37 of the reference: BM=BN=3 fails with 'PSUM'."""
+    from nkilab.kernels import matmul as mm
+
+    lhsT = np.zeros((128, 384), np.float32)
+    rhs = np.zeros((128, 1536), np.float32)
+    with pytest.raises(Exception, match="PSUM"):
+        mm.matmul_blocked(lhsT, rhs, BM=3, BN=3)
+
+
+def test_kernel_level_shape_asserts():
+    from nkilab.kernels import attention as at
+    from nkilab.kernels import matmul as mm
+
+    with pytest.raises(AssertionError):
+        mm.matmul_naive(np.zeros((100, 128), np.float32), np.zeros((100, 512), np.float32))
+    with pytest.raises(AssertionError):
+        at.flash_attention(np.zeros((1, 64, 100), np.float32), np.zeros((1, 64, 100), np.float32),
+                           np.zeros((1, 100, 64), np.float32), 0.125)
+
+
+def test_ops_argument_errors_before_any_device_work():
+    from nkilab import ops
+
+    with pytest.raises(AssertionError):
+        ops.matmul(np.zeros((4, 5), np.float32), np.zeros((6, 3), np.float32))
+    with pytest.raises(KeyError):
+        ops.attention(np.zeros((1, 4, 8), np.float32), np.zeros((1, 4, 8), np.float32),
+                      np.zeros((1, 4, 8), np.float32), variant="nope")
+    with pytest.raises(AssertionError):
+        ops.attention(np.zeros((1, 4, 256), np.float32), np.zeros((1, 4, 256), np.float32),
+                      np.zeros((1, 4, 256), np.float32))
+
+
+def test_attention_variants_keys_match_reference():
+    from nkilab import ops
+
+    assert list(ops.ATTENTION_VARIANTS) == ["naive", "flash", "flash_kv_resident", "flash_balanced",
+                                            "flash_pipelined"]
+
+
+def test_ops_refuse_cpu_execution():
+    """No CPU fallback: the custom ops raise on CPU tensors."""
+    import torch
+
+    from nkilab import _torch_ops  # noqa: F401
+
+    x = torch.zeros(4, 8)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        torch.ops.nkilab.softmax(x, True)
+
+
+def test_block_weights_follow_reference_seeding():
+    import torch
+
+    from nkilab.model import BlockConfig, DecoderBlock
+
+    torch.manual_seed(0)
+    b = DecoderBlock(BlockConfig())
+    names = [n for n, _ in b.named_parameters()]
+    assert names == ["norm1.weight", "norm2.weight", "wqkv.weight", "wo.weight", "wg.weight", "wu.weight", "wd.weight"]
+    assert float(b.norm1.weight.min()) >= 0.5 and float(b.norm1.weight.max()) <= 1.5

@@ -1,0 +1,83 @@
+"""GPU parity of the decoder block (nkilab.model.nki_forward on the CUDA kernels)."""
+from __future__ import annotations
+
+import ml_dtypes
+import numpy as np
+import pytest
+import torch
+
+from conftest import cases, load_golden, rel_err, to_numpy, to_torch
+from oracle import nki_oracle as O
+
+pytestmark = pytest.mark.gpu
+BF16 = ml_dtypes.bfloat16
+MODEL = load_golden("golden_model.npz")
+
+
+def _block(cfg=None, seed=0):
+    from nkilab.model import BlockConfig, DecoderBlock
+
+    torch.manual_seed(seed)
+    return DecoderBlock(cfg or BlockConfig()).eval()
+
+
+def _oracle(block, x):
+    return O.decoder_block(x, block.norm1.weight.detach(), block.wqkv.weight.detach(), block.wo.weight.detach(),
+                           block.norm2.weight.detach(), block.wg.weight.detach(), block.wu.weight.detach(),
+                           block.wd.weight.detach(), block.cfg.n_heads, block.cfg.eps)
+
+
+@pytest.mark.parametrize("case", cases(MODEL))
+def test_decoder_block_matches_reference(case):
+    from nkilab.model import nki_forward
+
+    block = _block()
+    x = MODEL[f"{case}/x"]
+    variant = "naive" if case.endswith("naive") else "flash_pipelined"
+    out = nki_forward(block, x, attention_variant=variant)
+    gold = MODEL[f"{case}/out_nki_forward"]
+    if gold.dtype == BF16:
+        assert out.dtype == BF16
+        assert rel_err(out.astype(np.float32), gold.astype(np.float32)) < 3e-3
+    else:
+        np.testing.assert_allclose(out, MODEL[f"{case}/out_torch_block"], atol=1e-5)
+        assert rel_err(out, gold) < 1e-5
+
+
+@pytest.mark.parametrize("S", [128, 300])
+@pytest.mark.parametrize("variant", ["naive", "flash_pipelined"])
+def test_decoder_block_matches_pytorch(S, variant):
+    """tests/test_model.py:8-17 of the reference."""
+    from nkilab.model import nki_forward
+
+    block = _block()
+    x = torch.randn(S, block.cfg.d_model)
+    with torch.no_grad():
+        ref = block(x).numpy()
+    np.testing.assert_allclose(nki_forward(block, x.numpy(), attention_variant=variant), ref, atol=1e-5)
+
+
+def test_decoder_block_device_batched_bf16():
+    """Device path with a batch dimension equals per-sequence oracle results."""
+    from nkilab.model import BlockConfig, nki_forward
+
+    block = _block(BlockConfig(d_model=512, n_heads=4, d_ff=1376))
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(2, 384, 512, generator=g).to(torch.bfloat16)
+    out = nki_forward(block, x.cuda())
+    assert out.shape == x.shape and out.dtype == torch.bfloat16
+    for b in range(2):
+        ref = _oracle(block, x[b])
+        assert rel_err(out[b].float().cpu().numpy(), ref.float().numpy()) < 3e-3
+
+
+def test_weight_cache_refreshes_on_update():
+    from nkilab.model import nki_forward
+
+    block = _block()
+    x = torch.randn(128, 256).cuda()
+    y1 = nki_forward(block, x)
+    with torch.no_grad():
+        block.wd.weight.mul_(0.0)
+    y2 = nki_forward(block, x)
+    assert not torch.equal(y1, y2)
