@@ -1,0 +1,502 @@
+"""Benchmark of the nkilab B200 kernel set (prints ONE JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Headline (BASELINE.json metric): causal flash attention, 8 heads x 2048 x 128, bf16,
+one forward per step, per GPU (weak scaling: every rank runs its own batch element;
+the attention path has no exchange step, so there is no collective in the timed
+region). Also reported on the same line: the three row kernels at [4096, 2048] bf16
+(HBM GB/s), the GEMM at 1024^3 and 8192^3 bf16, and the decoder block of BASELINE's
+configs[4], each against the measured roofline.
+
+value      K steps through torch.ops.nkilab.attention, captured in one CUDA graph,
+           inputs resident in HBM, rotating through a 256 MiB pool of input sets so
+           no step finds its inputs in the 126 MB L2; CUDA events on the launching
+           stream, barrier + synchronize on both sides, max over ranks.
+e2e        the same metric through the public API nkilab.ops.attention with pinned
+           host tensors: host->device copy of q, k, v and device->host copy of the
+           output inside every timed step.
+reference  --impl reference times the reference algorithm on the host cores: the
+           CPU port of the NKI kernels (oracle/nki_oracle.py), since the reference's
+           own CPU path (the NKI simulator) cannot be installed in this image.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "nki-kernel-lab_b200"))
+sys.path.insert(0, ROOT)
+
+import torch  # noqa: E402
+
+H, S, D = 8, 2048, 128
+ATTN_FLOP = 2.0 * H * S * S * D  # causal half of 4*H*S^2*d
+ROWS, COLS = 4096, 2048
+METRIC = "causal-attn TFLOPS (8×2048×128 bf16) + row-kernel HBM GB/s, % roofline"
+L2_BYTES = 126 * 1024 * 1024
+POOL_BYTES = 256 * 1024 * 1024
+
+
+def peaks() -> dict:
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
+                "source": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def ncu_traffic(kernel_file: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<kernel_file>."""
+    try:
+        with open(os.path.join(ROOT, "profiles", kernel_file)) as f:
+            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+        return float(m.group(1)) if m else None
+    except OSError:
+        return None
+
+
+# --------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join("/tmp", f"nkl_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=self.fh,
+                                         stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        loaded = [float(r[1]) for r in rows if r[3].replace(".", "").isdigit() and float(r[3]) > 250.0] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(loaded) if loaded else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------------------------- timing helpers
+
+def timed_graph(fn_step, n_steps: int, stream: torch.cuda.Stream) -> float:
+    """Capture n_steps calls of fn_step(i) in one CUDA graph; return elapsed ms of one
+    replay measured with CUDA events on `stream`."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(g, stream=stream):
+            for i in range(n_steps):
+                fn_step(i)
+    torch.cuda.synchronize()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        t0.record(stream)
+        g.replay()
+        t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    del g
+    return ms
+
+
+def warm(fn_step, n: int, stream):
+    with torch.cuda.stream(stream):
+        for i in range(n):
+            fn_step(i)
+    torch.cuda.synchronize()
+
+
+# --------------------------------------------------------------------------- our arm
+
+def bench_attention(steps: int, warmup: int, dev, stream, dist_ctx) -> dict:
+    per_set = 4 * H * S * D * 2
+    nset = max(2, math.ceil(POOL_BYTES / per_set))
+    g = torch.Generator(device=dev).manual_seed(1234 + dist_ctx["rank"])
+    pool = [tuple(torch.randn(H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
+            for _ in range(nset)]
+    scale = 1.0 / math.sqrt(D)
+
+    def step(i):
+        q, k, v = pool[i % nset]
+        torch.ops.nkilab.attention(q, k, v, scale, False)
+
+    warm(step, warmup, stream)
+    # clock soak: same load, untimed, so the 200 ms clock samples see the kernel running
+    t_end = time.time() + 1.5
+    while time.time() < t_end:
+        warm(step, 200, stream)
+    dist_ctx["barrier"]()
+    torch.cuda.synchronize()
+    ms = timed_graph(step, steps, stream)
+    torch.cuda.synchronize()
+    dist_ctx["barrier"]()
+    ms = dist_ctx["max"](ms)
+    return {"ms_total": ms, "ms_per_step": ms / steps, "pool_sets": nset, "pool_mib": nset * per_set / 2**20}
+
+
+def bench_rows(steps: int, warmup: int, dev, stream, pk) -> dict:
+    out = {}
+    g = torch.Generator(device=dev).manual_seed(7)
+    x_bytes = ROWS * COLS * 2
+    specs = {
+        "rmsnorm": (2, 2 * x_bytes + COLS * 2),
+        "softmax": (1, 2 * x_bytes),
+        "swiglu": (2, 3 * x_bytes),
+    }
+    for name, (n_in, alg_bytes) in specs.items():
+        nset = max(2, math.ceil(POOL_BYTES / (alg_bytes)))
+        sets = [[torch.randn(ROWS, COLS, device=dev, generator=g).to(torch.bfloat16) for _ in range(n_in)]
+                for _ in range(nset)]
+        gamma = (1 + 0.1 * torch.randn(COLS, device=dev, generator=g)).to(torch.bfloat16)
+
+        def step(i, name=name, sets=sets, gamma=gamma):
+            t = sets[i % len(sets)]
+            if name == "rmsnorm":
+                torch.ops.nkilab.rmsnorm(t[0], gamma, 1e-6)
+            elif name == "softmax":
+                torch.ops.nkilab.softmax(t[0], True)
+            else:
+                torch.ops.nkilab.swiglu(t[0], t[1])
+
+        warm(step, warmup, stream)
+        ms = timed_graph(step, steps, stream) / steps
+        gbs = alg_bytes / (ms * 1e-3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 3), "gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+                     "bytes_per_launch": alg_bytes, "pool_mib": round(nset * alg_bytes / 2**20)}
+        del sets
+    return out
+
+
+def bench_gemm(dev, stream, pk) -> dict:
+    out = {}
+    for n, steps in ((1024, 200), (8192, 10)):
+        g = torch.Generator(device=dev).manual_seed(n)
+        per = 3 * n * n * 2
+        nset = max(1, math.ceil(POOL_BYTES / per)) if n <= 4096 else 1
+        sets = [((torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(torch.bfloat16),
+                 (torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(torch.bfloat16)) for _ in range(nset)]
+
+        def step(i, sets=sets):
+            a, b = sets[i % len(sets)]
+            torch.ops.nkilab.matmul(a, b, False)
+
+        warm(step, 3, stream)
+        ms = timed_graph(step, steps, stream) / steps
+        tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
+        out[f"{n}^3"] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / pk["bf16_tflops"], 4)}
+        del sets
+    return out
+
+
+def bench_block(dev, stream, pk) -> dict:
+    from nkilab.model import BlockConfig, DecoderBlock, nki_forward
+
+    cfg = BlockConfig(d_model=4096, n_heads=32, d_ff=11008)
+    torch.manual_seed(0)
+    with torch.device("meta"):
+        block = DecoderBlock(cfg)
+    block = block.to_empty(device=dev)
+    with torch.no_grad():
+        for p in block.parameters():
+            p.normal_(0.0, 0.02)
+        block.norm1.weight.uniform_(0.5, 1.5)
+        block.norm2.weight.uniform_(0.5, 1.5)
+    B, Sb, d, f = 4, 4096, 4096, 11008
+    x = torch.randn(B, Sb, d, device=dev).to(torch.bfloat16)
+    flop = 2.0 * B * Sb * d * (3 * d + d + 2 * f) + 2.0 * B * Sb * f * d + 2.0 * B * 32 * Sb * Sb * 128
+    with torch.cuda.stream(stream):
+        for _ in range(2):
+            nki_forward(block, x)
+        torch.cuda.synchronize()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        steps = 3
+        t0.record(stream)
+        for _ in range(steps):
+            nki_forward(block, x)
+        t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    tf = flop / (ms * 1e-3) / 1e12
+    return {"config": "B=4 S=4096 d=4096 H=32x128 ff=11008 bf16", "ms": round(ms, 3), "tflops": round(tf, 1),
+            "frac": round(tf / pk["bf16_tflops_sustained"], 4), "flop": flop}
+
+
+def bench_e2e(steps: int, warmup: int, dev) -> dict:
+    from nkilab import ops
+
+    g = torch.Generator().manual_seed(99)
+    host = [torch.randn(H, S, D, generator=g).to(torch.bfloat16).pin_memory() for _ in range(3)]
+    for _ in range(max(3, warmup)):
+        ops.attention(*host)
+    torch.cuda.synchronize()
+    stream = torch.cuda.current_stream(dev)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    t0.record(stream)
+    for _ in range(steps):
+        out = ops.attention(*host)  # H2D of q, k, v; kernel; D2H of out (synchronous)
+    t1.record(stream)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    assert out.shape == (H, S, D)
+    return {"value": round(ATTN_FLOP / (ms * 1e-3) / 1e12, 3), "unit": "TFLOPS", "ms_per_step": round(ms, 4),
+            "h2d_bytes_per_step": 3 * H * S * D * 2, "d2h_bytes_per_step": H * S * D * 2}
+
+
+# --------------------------------------------------------------------------- CPU baselines
+
+def cpu_attention_baseline(budget_s: float = 12.0) -> dict:
+    """The reference algorithm on host cores: oracle port of flash_attention_pipelined
+    (tile-level restatement, fp32 with bf16 P) on the full 8 x 2048 x 128 workload,
+    repeated within a wall-clock budget; plus torch SDPA (the reference tests' own
+    PyTorch reference) on the same inputs."""
+    from oracle import nki_oracle as O
+
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(H, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    O.attention_flash(q[:1, :256], k[:1, :256], v[:1, :256])
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        O.attention_flash(q, k, v)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or reps >= 50:
+            break
+    port_tflops = ATTN_FLOP * reps / el / 1e12
+    qf, kf, vf = q.float(), k.float(), v.float()
+    torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True)
+    t0 = time.perf_counter()
+    n = 0
+    while time.perf_counter() - t0 < 3.0:
+        torch.nn.functional.scaled_dot_product_attention(qf, kf, vf, is_causal=True)
+        n += 1
+    sdpa_tflops = ATTN_FLOP * n / (time.perf_counter() - t0) / 1e12
+    return {"value": round(port_tflops, 5), "unit": "TFLOPS", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{reps} full steps of oracle flash attention 8x2048x128 (bf16 in, fp32 math) in {el:.1f} s",
+            "torch_sdpa_fp32_tflops": round(sdpa_tflops, 5), "host_cpus": os.cpu_count()}
+
+
+def cpu_rows_baseline() -> dict:
+    from oracle import nki_oracle as O
+
+    g = torch.Generator().manual_seed(6)
+    x = torch.randn(ROWS, COLS, generator=g).to(torch.bfloat16)
+    u = torch.randn(ROWS, COLS, generator=g).to(torch.bfloat16)
+    w = torch.ones(COLS).to(torch.bfloat16)
+    out = {}
+    for name, fn, nbytes in (("rmsnorm", lambda: O.rmsnorm(x, w), 2 * ROWS * COLS * 2 + COLS * 2),
+                             ("softmax", lambda: O.softmax_fused(x), 2 * ROWS * COLS * 2),
+                             ("swiglu", lambda: O.swiglu(x, u), 3 * ROWS * COLS * 2)):
+        fn()
+        t0, n = time.perf_counter(), 0
+        while time.perf_counter() - t0 < 1.0:
+            fn()
+            n += 1
+        out[name] = round(nbytes * n / (time.perf_counter() - t0) / 1e9, 3)
+    return {"unit": "GB/s", "cores": torch.get_num_threads(), "kind": "port", **out}
+
+
+# --------------------------------------------------------------------------- distributed plumbing
+
+def dist_setup(n_gpus: int) -> dict:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    ctx = {"world": world, "rank": rank, "local": local}
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        ctx["barrier"] = lambda: dist.barrier()
+
+        def mx(v: float) -> float:
+            t = torch.tensor([v], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            return float(t.item())
+
+        ctx["max"] = mx
+    else:
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        ctx["barrier"] = lambda: None
+        ctx["max"] = lambda v: v
+    return ctx
+
+
+def dist_teardown(ctx):
+    if ctx["world"] > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+# --------------------------------------------------------------------------- main
+
+def run_reference(args, ctx) -> None:
+    if ctx["rank"] != 0:
+        return
+    from oracle import nki_oracle as O
+
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.randn(H, S, D, generator=g).to(torch.bfloat16) for _ in range(3))
+    t0 = time.perf_counter()
+    for _ in range(min(args.warmup, 2)):
+        O.attention_flash(q, k, v)
+    per_step = (time.perf_counter() - t0) / max(1, min(args.warmup, 2))
+    steps = max(1, min(args.steps, int(120.0 / max(per_step, 1e-3))))  # keep the arm within ~2 minutes
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        O.attention_flash(q, k, v)
+    el = time.perf_counter() - t0
+    val = ATTN_FLOP * steps / el / 1e12
+    line = {"metric": METRIC, "value": round(val, 6), "unit": "TFLOPS", "n_gpus": args.gpus, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": round(el / steps * 1e3, 2), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+            "config": {"workload": "causal attention 8x2048x128 bf16 (BASELINE configs[3]) on host cores",
+                       "heads": H, "seq_len": S, "head_dim": D},
+            "cpu_baseline": {"value": round(val, 6), "unit": "TFLOPS", "cores": torch.get_num_threads(),
+                             "kind": "port",
+                             "sample": f"{steps} full steps of the CPU port of flash_attention_pipelined "
+                                       "(the NKI simulator, the reference's own CPU path, is not installable here)"},
+            "e2e": {"value": round(val, 6), "unit": "TFLOPS", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, ctx) -> None:
+    from nkilab import _native, ops  # noqa: F401  (loads the CUDA library, registers the ops)
+
+    dev = torch.device("cuda", ctx["local"])
+    pk = peaks()
+    stream = torch.cuda.Stream(dev)
+    extra_err = {}
+    with ClockSampler(ctx["local"]) as clk:
+        att = bench_attention(args.steps, args.warmup, dev, stream, ctx)
+        rows = gemm = block = None
+        if not args.headline_only:
+            try:
+                rows = bench_rows(200, 5, dev, stream, pk)
+            except Exception as e:  # report, keep the headline
+                extra_err["row_kernels"] = repr(e)
+            try:
+                gemm = bench_gemm(dev, stream, pk)
+            except Exception as e:
+                extra_err["gemm"] = repr(e)
+            try:
+                block = bench_block(dev, stream, pk)
+            except Exception as e:
+                extra_err["decoder_block"] = repr(e)
+    clocks = clk.summary()
+    e2e = bench_e2e(max(10, min(args.steps, 50)), args.warmup, dev)
+    _native.check_device(torch.cuda.current_stream(dev).cuda_stream)
+    e2e_val = ctx["max"](e2e["ms_per_step"])
+    e2e["value"] = round(ATTN_FLOP * ctx["world"] / (e2e_val * 1e-3) / 1e12, 3)
+    cpu = cpu_attention_baseline() if (ctx["rank"] == 0 and ctx["world"] == 1 and not args.no_cpu) else None
+    cpu_rows = cpu_rows_baseline() if (cpu is not None) else None
+    if ctx["rank"] != 0:
+        return
+    ms = att["ms_per_step"]
+    per_gpu_tflops = ATTN_FLOP / (ms * 1e-3) / 1e12
+    value = per_gpu_tflops * ctx["world"]
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "TFLOPS", "n_gpus": ctx["world"], "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "causal attention 8x2048x128 bf16, scale 1/sqrt(128) (BASELINE configs[3])",
+                   "heads": H, "seq_len": S, "head_dim": D, "batch_per_gpu": 1,
+                   "parallelism": f"replicas{ctx['world']}" if ctx["world"] > 1 else "single",
+                   "l2": f"rotating pool of {att['pool_sets']} input sets, {att['pool_mib']:.0f} MiB > 2x L2",
+                   "launch": "K steps in one CUDA graph via torch.ops.nkilab.attention"},
+        "roofline": {"bound": "tensor", "achieved": round(per_gpu_tflops, 2), "peak": pk["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(per_gpu_tflops / pk["bf16_tflops"], 4),
+                     "traffic": ncu_traffic("attn_fwd_bf16_8x2048x128.md"),
+                     "algorithmic_flop_per_launch": ATTN_FLOP, "peak_source": pk["source"] + " burst bf16"},
+        "clocks": clocks,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+    }
+    if rows:
+        line["row_kernels"] = {**rows, "peak_gbs": pk["hbm_gbs"], "peak_source": pk["source"]}
+    if gemm:
+        line["gemm"] = gemm
+    if block:
+        line["decoder_block"] = block
+    if cpu:
+        line["cpu_baseline"] = cpu
+        line["cpu_baseline_rows"] = cpu_rows
+    if extra_err:
+        line["errors"] = extra_err
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--headline-only", action="store_true", help="only the attention headline (for profiling)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        ctx = {"world": int(os.environ.get("WORLD_SIZE", "1")), "rank": int(os.environ.get("RANK", "0"))}
+        run_reference(args, ctx)
+        return
+    ctx = dist_setup(args.gpus)
+    try:
+        run_ours(args, ctx)
+    finally:
+        dist_teardown(ctx)
+
+
+if __name__ == "__main__":
+    main()

@@ -91,3 +91,20 @@ def bf16_ulp_diff(a, b) -> np.ndarray:
         u = np.asarray(x).view(np.uint16).astype(np.int32)
         return np.where(u & 0x8000, 0x8000 - (u & 0x7FFF), 0x8000 + u)
     return np.abs(key(a) - key(b))
+
+
+def bf16_spacing(v) -> np.ndarray:
+    """Gap between adjacent bf16 values at |v| (one ulp), elementwise."""
+    a = np.abs(np.asarray(v, dtype=np.float32))
+    return np.exp2(np.floor(np.log2(np.maximum(a, np.float32(2.0 ** -126)))) - 7)
+
+
+def bf16_excess_rel(a, b) -> float:
+    """rel_err after allowing each element one bf16 ulp for the final output rounding:
+    max(|a - b| - ulp(b), 0) / max|b|. Two correct bf16 pipelines that differ only in
+    fp32 accumulation order can disagree by one output ulp anywhere, which alone can
+    exceed a 3e-3 plain rel_err when |b| reaches 4; this metric measures the error the
+    computation adds beyond that unavoidable rounding."""
+    a = np.asarray(a, dtype=np.float32)
+    b = np.asarray(b, dtype=np.float32)
+    return float(np.maximum(np.abs(a - b) - bf16_spacing(b), 0).max() / max(np.abs(b).max(), 1e-12))
