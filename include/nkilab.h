@@ -87,6 +87,25 @@ size_t nkl_softmax_unfused_workspace_size(int64_t rows, int64_t cols);
 int nkl_softmax_unfused(const void* x, void* out, void* workspace, size_t workspace_bytes,
                         int64_t rows, int64_t cols, int dtype, void* stream);
 
+/* Allocation-free variant of nkl_softmax_unfused, for callers that cannot call
+ * cudaMalloc (a host that binds only this C ABI from a language runtime with no CUDA
+ * allocator binding, or that must stay inside a device-memory budget owned by another
+ * allocator). No counterpart in the reference, which has no device memory at all.
+ * Same result as nkl_softmax_unfused; its scratch (row maxima, row sums, fp32
+ * exponentials) is a fixed NKL_SOFTMAX_UNFUSED_STATIC_BYTES array in the library's
+ * device image, which every GPU that loads the library holds until the process exits.
+ * Inputs needing more than that (nkl_softmax_unfused_workspace_size(rows, cols) >
+ * NKL_SOFTMAX_UNFUSED_STATIC_BYTES, e.g. more than about 4M fp32 elements) are
+ * rejected with NKL_ERR_SHAPE and nothing is launched. The call allocates nothing.
+ * The first call on each device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call before any
+ * stream capture. All calls on a device share the one array and it keeps the last
+ * call's contents: calls whose kernels overlap on the GPU (different streams, or
+ * several host threads) race on it, so issue them on one stream. */
+#define NKL_SOFTMAX_UNFUSED_STATIC_BYTES (16u * 1024u * 1024u)
+int nkl_softmax_unfused_static(const void* x, void* out, int64_t rows, int64_t cols, int dtype,
+                               void* stream);
+
 /* y = silu(gate) * up, elementwise over [rows, cols], fp32 silu.
  * Replaces nkilab/ops.py:64-65 (swiglu) -> nkilab/kernels/norm.py:121-136 (swiglu_fused). */
 int nkl_swiglu(const void* gate, const void* up, void* out, int64_t rows, int64_t cols,

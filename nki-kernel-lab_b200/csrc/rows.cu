@@ -15,6 +15,8 @@
 // output dtype at the end (rmsnorm rounds x*rstd to fp32 before the weight multiply,
 // norm.py:114-116; fused softmax multiplies by a reciprocal, norm.py:84-87; unfused
 // softmax divides, norm.py:142).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace nkl {
@@ -428,4 +430,68 @@ extern "C" int nkl_swiglu(const void* gate, const void* up, void* out, int64_t r
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == NKL_FLOAT32 ? swiglu_launch<float>(gate, up, out, rows * cols, st)
                               : swiglu_launch<bf16>(gate, up, out, rows * cols, st);
+}
+
+// ------------------------------------------------------------------ allocation-free variant
+// nkl_softmax_unfused_static: the three-pass softmax above with its scratch (row maxima,
+// row sums, fp32 exponentials) in a fixed array that lives in this library's device
+// image instead of a caller-supplied workspace. It exists for callers that cannot call
+// cudaMalloc: hosts that bind only this C ABI from a language runtime with no CUDA
+// allocator binding, or that run inside a device-memory budget owned by another
+// allocator and may not take memory outside it.
+//
+// The array is NKL_SOFTMAX_UNFUSED_STATIC_BYTES (16 MiB). Every GPU that loads the
+// library holds it until the process exits. Its host-side name is only a stand-in for
+// the device symbol, so the device address is looked up with cudaGetSymbolAddress, once
+// per device, with that device current, on the first call made on that device.
+namespace nkl {
+namespace {
+
+__device__ __align__(256) unsigned char g_softmax_static_scratch[NKL_SOFTMAX_UNFUSED_STATIC_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_scratch_mu;
+void* g_static_scratch_addr[kMaxDevices] = {nullptr};
+
+// Device address of g_softmax_static_scratch on the current device (looked up once).
+int static_scratch_address(void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_softmax_unfused_static: cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(NKL_ERR_ARG, "nkl_softmax_unfused_static: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_static_scratch_mu);
+  if (g_static_scratch_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_softmax_static_scratch);
+    if (e != cudaSuccess || p == nullptr)
+      return fail(NKL_ERR_CUDA, "nkl_softmax_unfused_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    g_static_scratch_addr[dev] = p;
+  }
+  *out = g_static_scratch_addr[dev];
+  return NKL_OK;
+}
+
+}  // namespace
+}  // namespace nkl
+
+extern "C" int nkl_softmax_unfused_static(const void* x, void* out, int64_t rows, int64_t cols, int dtype,
+                                          void* stream) {
+  int rc = check_rows("nkl_softmax_unfused_static", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!x || !out) return fail(NKL_ERR_ARG, "nkl_softmax_unfused_static: NULL pointer");
+  const size_t need = nkl_softmax_unfused_workspace_size(rows, cols);
+  if (need > (size_t)NKL_SOFTMAX_UNFUSED_STATIC_BYTES)
+    return fail(NKL_ERR_SHAPE,
+                "nkl_softmax_unfused_static: [%lld, %lld] needs %zu B of scratch, above the fixed %zu B "
+                "(use nkl_softmax_unfused with a caller-owned workspace)",
+                (long long)rows, (long long)cols, need, (size_t)NKL_SOFTMAX_UNFUSED_STATIC_BYTES);
+  void* scratch = nullptr;
+  rc = static_scratch_address(&scratch);
+  if (rc) return rc;
+  // Every scratch byte a pass reads was written by an earlier pass of the same call,
+  // so the array needs no clearing between calls.
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  return dtype == NKL_FLOAT32 ? softmax_unfused_launch<float>(x, out, scratch, rows, cols, st)
+                              : softmax_unfused_launch<bf16>(x, out, scratch, rows, cols, st);
 }

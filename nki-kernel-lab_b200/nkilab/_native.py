@@ -41,6 +41,7 @@ SIGNATURES = {
     "nkl_softmax": (_int, [_p, _p, _i64, _i64, _int, _p]),
     "nkl_softmax_unfused_workspace_size": (_sz, [_i64, _i64]),
     "nkl_softmax_unfused": (_int, [_p, _p, _p, _sz, _i64, _i64, _int, _p]),
+    "nkl_softmax_unfused_static": (_int, [_p, _p, _i64, _i64, _int, _p]),
     "nkl_swiglu": (_int, [_p, _p, _p, _i64, _i64, _int, _p]),
     "nkl_matmul": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_naive": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
@@ -50,6 +51,7 @@ SIGNATURES = {
 }
 
 ABI_VERSION = 1
+SOFTMAX_UNFUSED_STATIC_BYTES = 16 * 1024 * 1024  # NKL_SOFTMAX_UNFUSED_STATIC_BYTES
 
 
 class NklError(RuntimeError):
