@@ -142,6 +142,23 @@ int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N
 int nkl_attention(const void* q, const void* k, const void* v, void* out, int64_t heads,
                   int64_t seq, int64_t head_dim, float scale, int dtype, void* stream);
 
+/* Bytes of workspace nkl_attention_ws uses for this shape on the current device
+ * (0 when the shape needs none: fp32, or enough query tiles to fill the GPU). */
+size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype);
+
+/* nkl_attention with a caller-owned workspace that lets the bf16 kernel split the
+ * causal key range of long query tiles into chunks spread over all SMs (split-KV);
+ * partial results are combined in a fixed chunk order, so the output is bit-identical
+ * for any scheduling. The workspace (>= nkl_attention_workspace_size bytes, 256-byte
+ * aligned) must be zero-filled before its first use; every call leaves it ready for
+ * the next. Calls that overlap on the GPU must not share a workspace. NULL workspace
+ * or fp32: same as nkl_attention.
+ * Replaces nkilab/ops.py:77-91 (attention, any "flash*" variant)
+ *   -> nkilab/kernels/attention.py:155-325. */
+int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, void* workspace,
+                     size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim,
+                     float scale, int dtype, void* stream);
+
 /* Bytes of device workspace nkl_attention_naive needs: fp32 scores and dtype
  * probabilities, each [heads, seq, seq]. */
 size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype);

@@ -137,12 +137,20 @@ softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, in
     }
   }
   const float neg_max = -warp_max(m);
+  // Rows of up to 64 values per lane keep exp(x - max) in registers, so each element
+  // costs one exp; longer rows recompute it in the output pass to bound registers.
+  constexpr bool kKeep = NV * V <= 64;
+  float ex[kKeep ? NV * V : 1];
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     if (i * 32 + lane < nvec) {
 #pragma unroll
-      for (int e = 0; e < V; ++e) s += row_exp<T>(xv[i].get(e) + neg_max);
+      for (int e = 0; e < V; ++e) {
+        const float t = row_exp<T>(xv[i].get(e) + neg_max);
+        if constexpr (kKeep) ex[i * V + e] = t;
+        s += t;
+      }
     }
   }
   const float rinv = 1.0f / warp_sum(s);
@@ -152,7 +160,10 @@ softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, in
     if (j < nvec) {
       float o[V];
 #pragma unroll
-      for (int e = 0; e < V; ++e) o[e] = row_exp<T>(xv[i].get(e) + neg_max) * rinv;
+      for (int e = 0; e < V; ++e) {
+        if constexpr (kKeep) o[e] = ex[i * V + e] * rinv;
+        else o[e] = row_exp<T>(xv[i].get(e) + neg_max) * rinv;
+      }
       st_stream(yr + (int64_t)j * V, pack16<T>(o));
     }
   }

@@ -25,6 +25,11 @@ namespace sm100 {
 
 constexpr uint64_t kWaitTimeoutNs = 1000ull * 1000ull * 1000ull;  // 1 s
 
+// Waiting threads poll with plain try_wait (0) or sleep up to this many ns per try.
+#ifndef NKL_MBAR_SLEEP_NS
+#define NKL_MBAR_SLEEP_NS 0
+#endif
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -72,21 +77,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended (up to `hint_ns`) until the phase
+// completes instead of returning at once: waiting lanes sleep rather than spin, so
+// they do not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait for the phase with the given parity to complete. Returns false (and sets
 // *abort) when the wait expired or another warp of the CTA already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
                                           unsigned int* dev_err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
+  for (;;) {
+#if NKL_MBAR_SLEEP_NS > 0
+    if (mbar_try_wait_sleep(bar, parity, NKL_MBAR_SLEEP_NS)) return true;
+#else
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 255u) == 0u) {
-      if (*abort) return false;
-      if (globaltimer() - t0 > kWaitTimeoutNs) {
-        *abort = 1;
-        atomicCAS(dev_err, 0u, (unsigned int)code);
-        return false;
-      }
+#endif
+    if (*abort) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      *abort = 1;
+      atomicCAS(dev_err, 0u, (unsigned int)code);
+      return false;
     }
   }
 }
@@ -126,6 +146,10 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void*
 __device__ __forceinline__ void tma_store_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void tma_store_wait_all() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Wait until every committed bulk store has finished reading its shared memory source.
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
 
 // Make generic-proxy shared memory writes visible to the async proxy (TMA store,

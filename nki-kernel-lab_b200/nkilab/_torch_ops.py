@@ -8,7 +8,7 @@ compose with streams and CUDA-graph capture like any torch op:
     torch.ops.nkilab.softmax(x, fused)              -> nkl_softmax / nkl_softmax_unfused
     torch.ops.nkilab.swiglu(gate, up)               -> nkl_swiglu
     torch.ops.nkilab.matmul(a, b, naive)            -> nkl_matmul / nkl_matmul_naive
-    torch.ops.nkilab.attention(q, k, v, scale, naive) -> nkl_attention / nkl_attention_naive
+    torch.ops.nkilab.attention(q, k, v, scale, naive) -> nkl_attention_ws / nkl_attention_naive
 
 There is no CPU implementation: a CPU tensor is an error, never a fallback.
 """
@@ -121,6 +121,21 @@ def _(a, b, naive):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
+# Split-KV workspaces of the bf16 attention kernel, one per (device, stream): zero-filled
+# once when created or grown; the kernel leaves them ready for the next call. Calls on
+# one stream are ordered, so they can share it; other streams get their own.
+_attention_ws: dict = {}
+
+
+def _attention_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    key = (dev.index, stream)
+    ws = _attention_ws.get(key)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        _attention_ws[key] = ws
+    return ws
+
+
 @torch.library.custom_op("nkilab::attention", mutates_args=())
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, naive: bool) -> torch.Tensor:
     dev, dt, st = _prep(q, k, v)
@@ -135,7 +150,14 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, n
             N.call("nkl_attention_naive", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ws.data_ptr(),
                    nbytes, H, S, d, scale, dt, st)
         else:
-            N.call("nkl_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, S, d, scale, dt, st)
+            nbytes = N.lib.nkl_attention_workspace_size(H, S, d, dt)
+            if nbytes:
+                ws = _attention_workspace(dev, st, nbytes)
+                N.call("nkl_attention_ws", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ws.data_ptr(),
+                       nbytes, H, S, d, scale, dt, st)
+            else:
+                N.call("nkl_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), H, S, d, scale,
+                       dt, st)
     return out
 
 
