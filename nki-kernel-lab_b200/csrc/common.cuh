@@ -113,6 +113,37 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Programmatic dependent launch. A kernel launched with launch_pdl() lets the next
+// kernel of the stream start launching as soon as every CTA of this one has begun
+// (launch_dependents), and waits for the previous kernel of the stream to complete and
+// publish its memory (wait) before it reads anything. Stream order is unchanged; what
+// overlaps is one kernel's launch latency and ramp with the previous kernel's drain.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
+               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e != cudaSuccess) {
+    (void)cudaGetLastError();  // a refused launch must not be reported again by the next call
+    return fail(NKL_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return NKL_OK;
+}
+
 // exp(x) for the row kernels: the accurate library expf for fp32 outputs (the
 // reference's fp32 tolerances are 1e-5), the fast hardware-approximate __expf when
 // the result is rounded to bf16 (its error is far below one bf16 ulp).

@@ -8,8 +8,11 @@
 // The reference tiles 128 rows onto SBUF partitions; on B200 a row maps to one warp
 // (rows up to 512 16-byte vectors) held entirely in registers, so every byte of the
 // input is read from HBM once and every output byte written once, with 16-byte
-// coalesced accesses. Rows that are too long or not 16-byte aligned fall back to a
-// block-per-row kernel that streams the row more than once (still exact).
+// coalesced accesses. A warp owns RPW consecutive rows and issues every load of all
+// of them before the first reduction, which keeps 16 KiB per warp in flight; kernels
+// are launched with programmatic dependent launch (launch_pdl). Rows that are too long
+// or not 16-byte aligned fall back to a block-per-row kernel that streams the row more
+// than once (still exact).
 //
 // Rounding points follow the reference: statistics in fp32, one rounding to the
 // output dtype at the end (rmsnorm rounds x*rstd to fp32 before the weight multiply,
@@ -22,51 +25,61 @@
 namespace nkl {
 namespace {
 
-constexpr int kWarpsPerBlock = 4;
+// Launch shapes (rows of up to 64 16-byte vectors per lane), chosen by measurement on
+// B200 at [4096, 2048] bf16: RMSNorm holds two rows per warp in flight; softmax keeps
+// one row per warp (its exponentials stay in registers).
+constexpr int kRmsWarpsPerBlock = 2, kRmsRowsPerWarp = 2;
+constexpr int kSoftmaxWarpsPerBlock = 4, kSoftmaxRowsPerWarp = 1;
 constexpr int kMaxVecPerLane = 16;  // 512 vectors per row: 4096 bf16 / 2048 fp32 columns
 
 // ------------------------------------------------------------------ RMSNorm
 
-template <typename T, int NV>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
-rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y,
-                    int64_t rows, int cols, float inv_cols, float eps) {
+template <typename T, int NV, int RPW>
+__global__ void __launch_bounds__(kRmsWarpsPerBlock * 32)
+rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int64_t rows, int cols,
+                    float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
-  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  pdl_enter();
+  const int64_t row0 = ((int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5)) * RPW;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  if (row0 >= rows) return;
   const int nvec = cols / V;
-  const T* xr = x + row * cols;
-  T* yr = y + row * cols;
-
-  Vec16<T> xv[NV];
+  Vec16<T> xv[RPW][NV];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
-    if (j < nvec) xv[i].raw = ld_stream(xr + (int64_t)j * V);
-    else xv[i].raw = make_uint4(0u, 0u, 0u, 0u);
+  for (int r = 0; r < RPW; ++r) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      if (row0 + r < rows && j < nvec) xv[r][i].raw = ld_stream(x + (row0 + r) * cols + (int64_t)j * V);
+      else xv[r][i].raw = make_uint4(0u, 0u, 0u, 0u);
+    }
   }
-  float ssq = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
+  for (int r = 0; r < RPW; ++r) {
+    if (row0 + r >= rows) break;
+    float ssq = 0.f;
 #pragma unroll
-    for (int e = 0; e < V; ++e) { const float f = xv[i].get(e); ssq += f * f; }
-  }
-  ssq = warp_sum(ssq);
-  const float rstd = rsqrtf(ssq * inv_cols + eps);
+    for (int i = 0; i < NV; ++i) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
-    if (j < nvec) {
-      Vec16<T> wv;
-      wv.raw = *reinterpret_cast<const uint4*>(w + (int64_t)j * V);
-      float o[V];
+      for (int e = 0; e < V; ++e) { const float f = xv[r][i].get(e); ssq += f * f; }
+    }
+    ssq = warp_sum(ssq);
+    const float rstd = rsqrtf(ssq * inv_cols + eps);
+    T* yr = y + (row0 + r) * cols;
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        const float xn = xv[i].get(e) * rstd;  // fp32 x * rstd, then * weight
-        o[e] = xn * wv.get(e);
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      if (j < nvec) {
+        Vec16<T> wv;
+        wv.raw = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)j * V));
+        float o[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          const float xn = xv[r][i].get(e) * rstd;  // fp32 x * rstd, then * weight
+          o[e] = xn * wv.get(e);
+        }
+        st_stream(yr + (int64_t)j * V, pack16<T>(o));
       }
-      st_stream(yr + (int64_t)j * V, pack16<T>(o));
     }
   }
 }
@@ -111,60 +124,66 @@ rmsnorm_block_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __rest
 
 // ------------------------------------------------------------------ fused softmax
 
-template <typename T, int NV>
-__global__ void __launch_bounds__(kWarpsPerBlock * 32)
+template <typename T, int NV, int RPW>
+__global__ void __launch_bounds__(kSoftmaxWarpsPerBlock * 32)
 softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols) {
   constexpr int V = Vec16<T>::N;
-  const int64_t row = (int64_t)blockIdx.x * kWarpsPerBlock + (threadIdx.x >> 5);
+  pdl_enter();
+  const int64_t row0 = ((int64_t)blockIdx.x * kSoftmaxWarpsPerBlock + (threadIdx.x >> 5)) * RPW;
   const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  if (row0 >= rows) return;
   const int nvec = cols / V;
-  const T* xr = x + row * cols;
-  T* yr = y + row * cols;
-
-  Vec16<T> xv[NV];
+  Vec16<T> xv[RPW][NV];
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
-    if (j < nvec) xv[i].raw = ld_stream(xr + (int64_t)j * V);
-  }
-  float m = -INFINITY;
+  for (int r = 0; r < RPW; ++r) {
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    if (i * 32 + lane < nvec) {
-#pragma unroll
-      for (int e = 0; e < V; ++e) m = fmaxf(m, xv[i].get(e));
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      if (row0 + r < rows && j < nvec) xv[r][i].raw = ld_stream(x + (row0 + r) * cols + (int64_t)j * V);
     }
   }
-  const float neg_max = -warp_max(m);
   // Rows of up to 64 values per lane keep exp(x - max) in registers, so each element
   // costs one exp; longer rows recompute it in the output pass to bound registers.
   constexpr bool kKeep = NV * V <= 64;
-  float ex[kKeep ? NV * V : 1];
-  float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    if (i * 32 + lane < nvec) {
+  for (int r = 0; r < RPW; ++r) {
+    if (row0 + r >= rows) break;
+    float m = -INFINITY;
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        const float t = row_exp<T>(xv[i].get(e) + neg_max);
-        if constexpr (kKeep) ex[i * V + e] = t;
-        s += t;
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane < nvec) {
+#pragma unroll
+        for (int e = 0; e < V; ++e) m = fmaxf(m, xv[r][i].get(e));
       }
     }
-  }
-  const float rinv = 1.0f / warp_sum(s);
+    const float neg_max = -warp_max(m);
+    float ex[kKeep ? NV * V : 1];
+    float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
-    if (j < nvec) {
-      float o[V];
+    for (int i = 0; i < NV; ++i) {
+      if (i * 32 + lane < nvec) {
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        if constexpr (kKeep) o[e] = ex[i * V + e] * rinv;
-        else o[e] = row_exp<T>(xv[i].get(e) + neg_max) * rinv;
+        for (int e = 0; e < V; ++e) {
+          const float t = row_exp<T>(xv[r][i].get(e) + neg_max);
+          if constexpr (kKeep) ex[i * V + e] = t;
+          s += t;
+        }
       }
-      st_stream(yr + (int64_t)j * V, pack16<T>(o));
+    }
+    const float rinv = 1.0f / warp_sum(s);
+    T* yr = y + (row0 + r) * cols;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      if (j < nvec) {
+        float o[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          if constexpr (kKeep) o[e] = ex[i * V + e] * rinv;
+          else o[e] = row_exp<T>(xv[r][i].get(e) + neg_max) * rinv;
+        }
+        st_stream(yr + (int64_t)j * V, pack16<T>(o));
+      }
     }
   }
 }
@@ -252,6 +271,7 @@ template <typename T>
 __global__ void __launch_bounds__(kSwigluThreads)
 swiglu_vec_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t nvec) {
   constexpr int V = Vec16<T>::N;
+  pdl_enter();
   const int64_t base = (int64_t)blockIdx.x * kSwigluThreads * kSwigluUnroll + threadIdx.x;
   Vec16<T> gv[kSwigluUnroll], uv[kSwigluUnroll];
 #pragma unroll
@@ -307,14 +327,17 @@ int rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int64_t 
   T* yp = static_cast<T*>(y);
   if (row_vectorizable<T>(cols, x, y, w)) {
     const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
-    const unsigned grid = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
     const int c = (int)cols;
+    const dim3 blk(kRmsWarpsPerBlock * 32);
+    auto grid = [&](int rpw) {
+      return dim3((unsigned)((rows + (int64_t)kRmsWarpsPerBlock * rpw - 1) / ((int64_t)kRmsWarpsPerBlock * rpw)));
+    };
     switch (nv) {
-      case 1: rmsnorm_warp_kernel<T, 1><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
-      case 2: rmsnorm_warp_kernel<T, 2><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
-      case 4: rmsnorm_warp_kernel<T, 4><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
-      case 8: rmsnorm_warp_kernel<T, 8><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
-      default: rmsnorm_warp_kernel<T, 16><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, wp, yp, rows, c, inv_cols, eps); break;
+      case 1: return launch_pdl(rmsnorm_warp_kernel<T, 1, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
+      case 2: return launch_pdl(rmsnorm_warp_kernel<T, 2, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
+      case 4: return launch_pdl(rmsnorm_warp_kernel<T, 4, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
+      case 8: return launch_pdl(rmsnorm_warp_kernel<T, 8, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
+      default: return launch_pdl(rmsnorm_warp_kernel<T, 16, 1>, grid(1), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
     }
   } else {
     rmsnorm_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, wp, yp, rows, cols, inv_cols, eps);
@@ -328,14 +351,18 @@ int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStrea
   T* yp = static_cast<T*>(y);
   if (row_vectorizable<T>(cols, x, y, nullptr)) {
     const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
-    const unsigned grid = (unsigned)((rows + kWarpsPerBlock - 1) / kWarpsPerBlock);
     const int c = (int)cols;
+    const dim3 blk(kSoftmaxWarpsPerBlock * 32);
+    auto grid = [&](int rpw) {
+      return dim3(
+          (unsigned)((rows + (int64_t)kSoftmaxWarpsPerBlock * rpw - 1) / ((int64_t)kSoftmaxWarpsPerBlock * rpw)));
+    };
     switch (nv) {
-      case 1: softmax_warp_kernel<T, 1><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
-      case 2: softmax_warp_kernel<T, 2><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
-      case 4: softmax_warp_kernel<T, 4><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
-      case 8: softmax_warp_kernel<T, 8><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
-      default: softmax_warp_kernel<T, 16><<<grid, kWarpsPerBlock * 32, 0, st>>>(xp, yp, rows, c); break;
+      case 1: return launch_pdl(softmax_warp_kernel<T, 1, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
+      case 2: return launch_pdl(softmax_warp_kernel<T, 2, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
+      case 4: return launch_pdl(softmax_warp_kernel<T, 4, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
+      case 8: return launch_pdl(softmax_warp_kernel<T, 8, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
+      default: return launch_pdl(softmax_warp_kernel<T, 16, 1>, grid(1), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
     }
   } else {
     softmax_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, yp, rows, cols);
@@ -369,7 +396,7 @@ int swiglu_launch(const void* g, const void* u, void* y, int64_t n, cudaStream_t
     const int64_t nvec = n / V;
     const int64_t per_block = (int64_t)kSwigluThreads * kSwigluUnroll;
     const unsigned grid = (unsigned)((nvec + per_block - 1) / per_block);
-    swiglu_vec_kernel<T><<<grid, kSwigluThreads, 0, st>>>(gp, up, yp, nvec);
+    return launch_pdl(swiglu_vec_kernel<T>, dim3(grid), dim3(kSwigluThreads), 0, st, "nkl_swiglu", gp, up, yp, nvec);
   } else {
     int64_t blocks = (n + 255) / 256;
     const int64_t cap = (int64_t)sm_count() * 8;
