@@ -10,21 +10,34 @@
 // dtype=vdtype), key tiles after the diagonal skipped (:166), final O * (1/l) rounded
 // once (:137-142). The running max is kept in the log2 domain (scale * log2(e) folded
 // into one FMA before a hardware exp2); mathematically the same exp(scale*s - m).
+// The reference rescales O on every key tile; here O is rescaled only when a row's
+// running max grows by more than 2^8 (P values stay <= 256, exact in fp32 and
+// relatively exact in bf16), which gives the same softmax up to rounding.
 //
-// bf16 kernel (sm_100a), one CTA per (head, 128-query tile), heavy tiles first:
-//   warps 0-7  softmax. Thread = (query row, half): row r = 32*(warp%4) + lane is its
-//              TMEM lane; half = warp/4 owns score columns [64*half, 64*half + 64) and
-//              output columns [D/2*half, D/2*(half+1)). Per key tile: one tcgen05.ld
-//              batch of its 64 S columns, row max exchanged with the other half through
-//              shared memory (mbarrier-synchronised), exp2 with the scale folded into
-//              one FMA, P (bf16) into its 64-key sub-tile of a double-buffered shared P
-//              tile (UMMA K-major 128-byte swizzle), then O(j-1) = O(j-2)*corr + P(j-1).V
-//              from TMEM (deferred one tile, so the tensor core runs P.V(j-1) and S(j+1)
-//              while softmax(j) runs). Row sums stay per half until the end.
-//   warp 8     TMA producer: Q once, K and V tiles through separate 2-deep rings
-//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer
-//   TMEM       S double buffer (2 x 128 fp32 columns) + P.V double buffer (2 x d)
+// bf16 kernel (sm_100a): persistent, one CTA per SM, two softmax engines per CTA.
+//   work unit  (head, query-tile pair 2p / 2p+1, chunk of the causal key range); the
+//              host orders units longest first and assigns them to CTAs greedily
+//              (LPT); query tiles whose key range is split over several units write
+//              partial (O, max, sum) to a workspace and the chunk that finishes last
+//              combines them in chunk order (result independent of finish order)
+//   warps 0-3  engine 0 (query tile 2p), warps 4-7 engine 1 (tile 2p+1); thread =
+//              query row = TMEM lane. Per key tile: tcgen05.ld of the 128 scores, row
+//              max, lazy rescale of O in TMEM, exp2 with the scale folded into one FMA,
+//              P (bf16 pairs) written back over the score columns with tcgen05.st
+//   warp 8     TMA producer: Q of both engines per unit, K and V tiles through 2-deep
+//              rings shared by the engines
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer, interleaving the
+//              engines: S_e = Q_e K^T (smem x smem), O_e += P_e V (P from TMEM)
+//   TMEM       S/P of engine 0 [0,128), engine 1 [128,256), O_0 [256,256+d), O_1 after
+//   epilogue   O from TMEM, * 1/l, bf16, staged in the engine's Q buffer, TMA store
+#include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 #include <type_traits>
+#include <vector>
+
+#include <cuda_fp16.h>
 
 #include "common.cuh"
 #include "sm100.cuh"
@@ -38,11 +51,15 @@ __device__ unsigned int g_attn_dev_error = 0;
 using namespace sm100;
 
 constexpr int kTile = 128;  // query / key tile, as the reference's T (attention.py:24)
-constexpr int kSoftmaxThreads = 256;
-constexpr int kAttnThreads = kSoftmaxThreads + 64;
+constexpr int kEngineThreads = 128;
+constexpr int kAttnThreads = 2 * kEngineThreads + 64;
 constexpr int kProducerWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
+constexpr int kMaxCtas = 192;         // schedule table capacity (>= SMs of any sm_100 part)
+constexpr int kMaxSched = 1024;       // units listed explicitly; more units: round-robin
+constexpr int kMaxChunks = 4;         // a query tile's key range is split into at most 4 units
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -50,29 +67,80 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
 template <int D>
 struct AttnSmem {
-  static constexpr int kQBytes = kTile * D * 2;
-  uint8_t q[kQBytes];              // D/64 sub-tiles of [128 rows x 128 B]
-  uint8_t k[2][kQBytes];           // key tiles, K-major (head_dim contiguous)
-  uint8_t v[2][kQBytes];           // value tiles, N-major for the P.V product
-  uint8_t p[2][kTile * kTile * 2];  // P double buffer, each 2 sub-tiles of [128 rows x 64 keys]
-  float red[2][2][kTile];          // [slot][half][row]: row-max exchange, then the final row sums
-  uint64_t q_full;
+  static constexpr int kTileBytes = kTile * D * 2;
+  uint8_t q[2][kTileBytes];  // per engine: D/64 sub-tiles of [128 rows x 128 B]; output staging
+  uint8_t k[2][kTileBytes];  // key ring, K-major (head_dim contiguous)
+  uint8_t v[2][kTileBytes];  // value ring, N-major for the P.V product
+  uint64_t q_full[2], q_empty[2];
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2];
-  uint64_t p_full[2];
-  uint64_t pv_full[2], pv_free[2];
-  uint64_t xchg[2];
+  uint64_t s_full[2], p_full[2], pv_done[2], o_free[2];
+  uint64_t eng_sync[2];  // engine-local barrier (128 arrivals) for the epilogue
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  int flag[2];
 };
 
 template <int D>
 constexpr size_t attn_smem_bytes() {
   return sizeof(AttnSmem<D>);
+}
+
+// ---- split-KV work units over query-tile pairs
+struct AttnArgs {
+  unsigned char* ws;  // NULL when no query tile is split
+  int heads, q_tiles, pairs, chunk, units;
+  float scale_log2;
+  size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (max, sum) and O regions
+  int n_ctas_listed;              // > 0: cta_off / unit_list give each CTA's units
+  uint16_t cta_off[kMaxCtas + 1];
+  uint16_t unit_list[kMaxSched];
+};
+
+struct Unit {
+  int head, pm, chunk, n_chunks, j0, n, v0;  // v0: per-head index of this pair's chunk 0
+};
+
+__host__ __device__ __forceinline__ int pair_tiles(int pm, int q_tiles) {
+  return (2 * pm + 2 < q_tiles) ? 2 * pm + 2 : q_tiles;
+}
+
+// Unit index -> (head, pair, chunk). Units run head-fastest; pairs longest first; chunks ascending.
+__host__ __device__ __forceinline__ Unit decode_unit(int u, int heads, int pairs, int q_tiles, int C) {
+  Unit r;
+  r.head = u % heads;
+  int v = u / heads, base = 0;
+  for (int pm = pairs - 1; pm >= 0; --pm) {
+    const int nt = pair_tiles(pm, q_tiles);
+    const int c = (nt + C - 1) / C;
+    if (v < base + c) {
+      r.pm = pm;
+      r.chunk = v - base;
+      r.n_chunks = c;
+      r.j0 = r.chunk * C;
+      r.n = (C < nt - r.j0) ? C : nt - r.j0;
+      r.v0 = base;
+      return r;
+    }
+    base += c;
+  }
+  r.pm = -1;
+  return r;
 }
 
 // Wait by lane 0, then broadcast, so the whole warp stays converged for the
@@ -83,47 +151,22 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// ---- split-KV work units
-// A unit is (head, query tile qt, key chunk k): key tiles [k*C, min((k+1)*C, qt+1)) of
-// the causal range of query tile qt, for a chunk size C chosen on the host so that
-// there are enough units to fill every SM. Units are numbered head-fastest, query
-// tiles in descending order (longest first), chunks ascending, so the block scheduler
-// hands the largest units out first. Query tiles split into several chunks write
-// partial (O, running max, row sum) to the workspace; the chunk that finishes last
-// combines them in chunk order, so the result does not depend on finish order.
-
-// sum_{s=1..n} ceil(s / C): number of units of query tiles 0..n-1.
-__host__ __device__ __forceinline__ int units_below(int n, int C) {
-  const int a = n / C, b = n % C;
-  return C * a * (a + 1) / 2 + b * (a + 1);
-}
-
-// Unit index within a head -> (query tile, chunk).
-__device__ __forceinline__ void decode_unit(int u, int q_tiles, int C, int& qt, int& chunk) {
-  const int total = units_below(q_tiles, C);
-  int lo = 0, hi = q_tiles - 1;  // smallest qt with units_below(qt + 1) >= total - u
-  while (lo < hi) {
-    const int mid = (lo + hi) >> 1;
-    if (units_below(mid + 1, C) >= total - u) hi = mid;
-    else lo = mid + 1;
+__device__ __forceinline__ int unit_of(const AttnArgs& a, int i, int& u) {
+  if (a.n_ctas_listed > 0) {
+    const int k = a.cta_off[blockIdx.x] + i;
+    if (k >= a.cta_off[blockIdx.x + 1]) return 0;
+    u = a.unit_list[k];
+    return 1;
   }
-  qt = lo;
-  chunk = u - (total - units_below(qt + 1, C));
+  u = (int)blockIdx.x + i * (int)gridDim.x;
+  return u < a.units;
 }
-
-struct AttnArgs {
-  bf16* out;
-  unsigned char* ws;     // NULL when every query tile is a single unit
-  int heads, seq, q_tiles, chunk, units_per_head;
-  float scale_log2;
-  size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (m, l) and O regions
-};
 
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
-                     const AttnArgs args) {
+                     const __grid_constant__ AttnArgs args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {  // the swizzled tiles need a 1024-byte-aligned base
     if (threadIdx.x == 0) atomicCAS(&g_attn_dev_error, 0u, 40u);
@@ -131,38 +174,30 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   }
   auto& s = *reinterpret_cast<AttnSmem<D>*>(smem_raw);
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kSCol0 = 0;               // S buffers at columns [0,128) and [128,256)
-  constexpr uint32_t kPVCol0 = 2 * kTile;      // P.V buffers at [256, 256+D) and [256+D, 256+2D)
+  constexpr uint32_t kOCol0 = 2 * kTile;  // O_e at 256 + e*D
   constexpr uint32_t kIdescS = idesc_bf16_f32(kTile, kTile, false, false);
   constexpr uint32_t kIdescPV = idesc_bf16_f32(kTile, D, false, true);
   constexpr uint32_t kTileBytes = kTile * D * 2;
   constexpr int kSub = D / 64;  // 64-column (128-byte) sub-tiles per Q/K/V tile
-  constexpr int kHalfD = D / 2;
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int heads = args.heads;
+  const int heads = args.heads, q_tiles = args.q_tiles;
   const float scale_log2 = args.scale_log2;
-  const int head = (int)(blockIdx.x % (unsigned)heads);
-  int qt, chunk;
-  decode_unit((int)(blockIdx.x / (unsigned)heads), args.q_tiles, args.chunk, qt, chunk);
-  const int n_chunks = (qt + args.chunk) / args.chunk;  // ceil((qt + 1) / C)
-  const int j0 = chunk * args.chunk;                    // first key tile of this unit
-  const int n_kv = min(args.chunk, qt + 1 - j0);         // causal: tiles after qt are fully masked
-  const int q0 = qt * kTile;
 
   if (threadIdx.x == 0) {
-    mbar_init(&s.q_full, 1);
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&s.q_full[i], 1);
+      mbar_init(&s.q_empty[i], 1);
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
       mbar_init(&s.v_full[i], 1);
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
-      mbar_init(&s.p_full[i], kSoftmaxThreads);
-      mbar_init(&s.pv_full[i], 1);
-      mbar_init(&s.pv_free[i], kSoftmaxThreads);
-      mbar_init(&s.xchg[i], kSoftmaxThreads);
+      mbar_init(&s.p_full[i], kEngineThreads);
+      mbar_init(&s.pv_done[i], 1);
+      mbar_init(&s.o_free[i], kEngineThreads);
+      mbar_init(&s.eng_sync[i], kEngineThreads);
     }
     mbar_init(&s.mma_done, 1);
     s.abort = 0;
@@ -183,321 +218,383 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   if (warp == kProducerWarp) {
     // ------------------------------------------------ TMA producer
     if (elect_one()) {
-      int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1};
+      uint32_t kc = 0, vc = 0, qc[2] = {0, 0};
+      int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1}, q_armed[2] = {-1, -1};
       bool ok = true;
-      mbar_arrive_expect_tx(&s.q_full, kTileBytes);
-      for (int c = 0; c < kSub; ++c) tma_load_3d(s.q + c * (kTile * 128), &map_q, &s.q_full, c * 64, q0, head);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        if (!mbar_wait(&s.k_empty[st], ph ^ 1u, &s.abort, &g_attn_dev_error, 11)) { ok = false; break; }
-        mbar_arrive_expect_tx(&s.k_full[st], kTileBytes);
-        k_armed[st] = (int)ph;
+      int u;
+      // Per unit: K/V tile 0 first (their slots free up as soon as the previous unit's
+      // MMAs consume them), then the engines' Q tiles (their buffers free up only after
+      // the previous unit's output has been staged and stored), then the remaining K/V.
+      auto load_kv = [&](const Unit& un, int t) -> bool {
+        const int j = un.j0 + t;
+        const int ks = kc & 1;
+        if (!mbar_wait(&s.k_empty[ks], ((kc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 11)) return false;
+        mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
+        k_armed[ks] = (int)((kc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.k[st] + c * (kTile * 128), &map_k, &s.k_full[st], c * 64, (j0 + j) * kTile, head);
-        if (!mbar_wait(&s.v_empty[st], ph ^ 1u, &s.abort, &g_attn_dev_error, 12)) { ok = false; break; }
-        mbar_arrive_expect_tx(&s.v_full[st], kTileBytes);
-        v_armed[st] = (int)ph;
+          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, j * kTile, un.head);
+        ++kc;
+        const int vs = vc & 1;
+        if (!mbar_wait(&s.v_empty[vs], ((vc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 12)) return false;
+        mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
+        v_armed[vs] = (int)((vc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.v[st] + c * (kTile * 128), &map_v, &s.v_full[st], c * 64, (j0 + j) * kTile, head);
+          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, j * kTile, un.head);
+        ++vc;
+        return true;
+      };
+      for (int i = 0; ok && unit_of(args, i, u); ++i) {
+        const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
+        ok = load_kv(un, 0);
+        for (int e = 0; e < 2 && ok; ++e) {
+          const int qe = 2 * un.pm + e;
+          if (qe >= q_tiles || qe < un.j0) continue;  // engine has no query tile / no key in this unit
+          if (!mbar_wait(&s.q_empty[e], (qc[e] & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) { ok = false; break; }
+          mbar_arrive_expect_tx(&s.q_full[e], kTileBytes);
+          q_armed[e] = (int)(qc[e] & 1u);
+          for (int c = 0; c < kSub; ++c)
+            tma_load_3d(s.q[e] + c * (kTile * 128), &map_q, &s.q_full[e], c * 64, qe * kTile, un.head);
+          ++qc[e];
+        }
+        for (int t = 1; t < un.n && ok; ++t) ok = load_kv(un, t);
       }
       if (!ok) {  // let issued copies land before shared memory is released
         const uint64_t t0 = globaltimer();
-        while (!mbar_try_wait(&s.q_full, 0) && globaltimer() - t0 < kWaitTimeoutNs) {}
-        for (int i = 0; i < 2; ++i) {
-          if (k_armed[i] >= 0)
-            while (!mbar_try_wait(&s.k_full[i], (uint32_t)k_armed[i]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-          if (v_armed[i] >= 0)
-            while (!mbar_try_wait(&s.v_full[i], (uint32_t)v_armed[i]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+        for (int e = 0; e < 2; ++e) {
+          if (q_armed[e] >= 0)
+            while (!mbar_try_wait(&s.q_full[e], (uint32_t)q_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+          if (k_armed[e] >= 0)
+            while (!mbar_try_wait(&s.k_full[e], (uint32_t)k_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+          if (v_armed[e] >= 0)
+            while (!mbar_try_wait(&s.v_full[e], (uint32_t)v_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
         }
       }
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (elect_one()) {
-      bool ok = mbar_wait(&s.q_full, 0, &s.abort, &g_attn_dev_error, 21);
-      const uint32_t q_base = smem_u32(s.q);
-      // S(j) = Q K(j)^T into S buffer j&1.
-      auto issue_s = [&](int j) -> bool {
-        const int st = j & 1;
-        if (!mbar_wait(&s.k_full[st], (uint32_t)(j >> 1) & 1u, &s.abort, &g_attn_dev_error, 22)) return false;
-        tc_fence_after();
-        const uint32_t k_base = smem_u32(s.k[st]);
+      uint32_t kc = 0, vc = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+      const uint64_t q_desc0 = smem_desc_sw128(smem_u32(s.q[0]), 16, 1024);
+      const uint64_t q_desc1 = smem_desc_sw128(smem_u32(s.q[1]), 16, 1024);
+      const uint64_t k_desc0 = smem_desc_sw128(smem_u32(s.k[0]), 16, 1024);
+      const uint64_t k_desc1 = smem_desc_sw128(smem_u32(s.k[1]), 16, 1024);
+      const uint64_t v_desc0 = smem_desc_sw128(smem_u32(s.v[0]), kTile * 128, 1024);
+      const uint64_t v_desc1 = smem_desc_sw128(smem_u32(s.v[1]), kTile * 128, 1024);
+      bool ok = true;
+      // S_e = Q_e K^T for the K stage ks
+      auto issue_s = [&](int e, int ks) {
+        const uint64_t qd = e ? q_desc1 : q_desc0;
+        const uint64_t kd = ks ? k_desc1 : k_desc0;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (uint32_t)((kk >> 2) * (kTile * 128) + (kk & 3) * 32);
-          mma_bf16_ss(tmem + kSCol0 + (uint32_t)(st * kTile), smem_desc_sw128(q_base + off, 16, 1024),
-                      smem_desc_sw128(k_base + off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
+          const uint32_t off = (uint32_t)(((kk >> 2) * (kTile * 128) + (kk & 3) * 32) >> 4);
+          mma_bf16_ss(tmem + (uint32_t)(e * kTile), qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&s.k_empty[st]);
-        mma_commit(&s.s_full[st]);
-        return true;
+        mma_commit(&s.s_full[e]);
       };
-      if (ok) ok = issue_s(0);
-      if (ok && n_kv > 1) ok = issue_s(1);
-      for (int j = 0; j < n_kv && ok; ++j) {
-        const int b = j & 1;
-        const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-        // p_full(b) also means the softmax warps finished reading S buffer b.
-        if (!mbar_wait(&s.p_full[b], ph, &s.abort, &g_attn_dev_error, 23)) { ok = false; break; }
-        if (!mbar_wait(&s.v_full[b], ph, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
-        if (j >= 2 && !mbar_wait(&s.pv_free[b], ph ^ 1u, &s.abort, &g_attn_dev_error, 25)) { ok = false; break; }
-        tc_fence_after();
-        const uint32_t p_base = smem_u32(s.p[b]);
-        const uint32_t v_base = smem_u32(s.v[b]);
-#pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk) {
-          const uint32_t a_off = (uint32_t)((kk >> 2) * (kTile * 128) + (kk & 3) * 32);
-          const uint32_t b_off = (uint32_t)(kk * 2048);
-          mma_bf16_ss(tmem + kPVCol0 + (uint32_t)(b * D), smem_desc_sw128(p_base + a_off, 16, 1024),
-                      smem_desc_sw128(v_base + b_off, kTile * 128, 1024), kIdescPV, kk > 0 ? 1u : 0u);
+      int u;
+      for (int i = 0; ok && unit_of(args, i, u); ++i) {
+        const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
+        int na[2];  // key tiles of this unit each engine takes part in
+        for (int e = 0; e < 2; ++e) {
+          const int qe = 2 * un.pm + e;
+          na[e] = (qe >= q_tiles) ? 0 : max(0, min(un.n, qe + 1 - un.j0));
         }
-        mma_commit(&s.v_empty[b]);
-        mma_commit(&s.pv_full[b]);
-        if (j + 2 < n_kv) ok = issue_s(j + 2);
+        for (int e = 0; e < 2 && ok; ++e) {
+          if (!na[e]) continue;
+          ok = mbar_wait(&s.q_full[e], qc[e] & 1u, &s.abort, &g_attn_dev_error, 20);
+          ++qc[e];
+        }
+        if (!ok) break;
+        // S for tile 0
+        {
+          const int ks = kc & 1;
+          if (!mbar_wait(&s.k_full[ks], (kc >> 1) & 1u, &s.abort, &g_attn_dev_error, 21)) break;
+          tc_fence_after();
+          for (int e = 0; e < 2; ++e)
+            if (na[e] > 0) issue_s(e, ks);
+          mma_commit(&s.k_empty[ks]);
+        }
+        for (int t = 0; t < un.n && ok; ++t) {
+          const uint32_t kn = kc + (uint32_t)t + 1;  // ring index of the next K tile
+          const uint32_t vi = vc + (uint32_t)t;
+          const int vs = vi & 1;
+          bool v_ready = false, k_ready = false;
+          for (int e = 0; e < 2 && ok; ++e) {
+            if (t >= na[e]) continue;
+            if (!mbar_wait(&s.p_full[e], pc[e] & 1u, &s.abort, &g_attn_dev_error, 22)) { ok = false; break; }
+            ++pc[e];
+            if (t == 0 && !mbar_wait(&s.o_free[e], (oc[e] & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 23)) {
+              ok = false;
+              break;
+            }
+            if (!v_ready) {
+              if (!mbar_wait(&s.v_full[vs], (vi >> 1) & 1u, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
+              v_ready = true;
+            }
+            tc_fence_after();
+            const uint64_t vd = vs ? v_desc1 : v_desc0;
+            const uint32_t p_tmem = tmem + (uint32_t)(e * kTile);
+#pragma unroll
+            for (int kk = 0; kk < kTile / 16; ++kk)
+              mma_bf16_ts(tmem + kOCol0 + (uint32_t)(e * D), p_tmem + (uint32_t)(kk * 8), vd + (uint32_t)(kk * 128),
+                          kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+            if (t == na[e] - 1) {
+              mma_commit(&s.pv_done[e]);
+              ++oc[e];
+            }
+            if (t + 1 < na[e]) {  // next S of this engine, right behind its P.V (S/P columns reused)
+              if (!k_ready) {
+                if (!mbar_wait(&s.k_full[kn & 1], (kn >> 1) & 1u, &s.abort, &g_attn_dev_error, 25)) {
+                  ok = false;
+                  break;
+                }
+                k_ready = true;
+                tc_fence_after();
+              }
+              issue_s(e, kn & 1);
+            }
+          }
+          if (!ok) break;
+          mma_commit(&s.v_empty[vs]);
+          if (k_ready) mma_commit(&s.k_empty[kn & 1]);
+        }
+        kc += (uint32_t)un.n;
+        vc += (uint32_t)un.n;
       }
+      // Every MMA issued by this thread has completed once mma_done flips.
       mma_commit(&s.mma_done);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(&s.mma_done, 0) && globaltimer() - t0 < kWaitTimeoutNs) {}
     }
   } else {
-    // ------------------------------------------------ softmax (warps 0..7)
-    const int half = warp >> 2;
+    // ------------------------------------------------ softmax engines (warps 0-3, 4-7)
+    const int e = warp >> 2;
     const int r = (warp & 3) * 32 + lane;  // query row within the tile == TMEM lane
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const int c0 = half * 64;  // first score column of this thread
-    float2 o[kHalfD / 2];
-#pragma unroll
-    for (int i = 0; i < kHalfD / 2; ++i) o[i] = make_float2(0.f, 0.f);
-    float m = -INFINITY, l = 0.f, corr_prev = 0.f;
-    bool ok = true;
+    const uint32_t s_addr = tmem + lane_off + (uint32_t)(e * kTile);
+    const uint32_t o_addr = tmem + lane_off + kOCol0 + (uint32_t)(e * D);
     const int sw = r & 7;
     const float2 sc2 = make_float2(scale_log2, scale_log2);
-
-    // One key tile: row max, exp2, row sum and the bf16 P sub-tile. The diagonal tile
-    // (the only one with masked keys) is a separate instantiation so the others carry
-    // no per-element predicates.
-    auto softmax_tile = [&](auto diag_tag, const uint32_t (&v)[64], int b, float& corr_out) -> bool {
-      constexpr bool kDiag = decltype(diag_tag)::value;
-      const uint32_t ph = 0;  // unused; phases are passed through the waits below
-      (void)ph;
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    uint32_t sc = 0, dc = 0, xc = 0;
+    bool ok = true;
+    int u;
+    for (int i = 0; ok && unit_of(args, i, u); ++i) {
+      const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
+      const int qe = 2 * un.pm + e;
+      const int na = (qe >= q_tiles) ? 0 : max(0, min(un.n, qe + 1 - un.j0));
+      if (na == 0) continue;
+      float m_ref = -INFINITY, l = 0.f;
+      for (int t = 0; t < na; ++t) {
+        const int j = un.j0 + t;
+        if (!warp_wait(&s.s_full[e], sc & 1u, &s.abort, 31)) { ok = false; break; }
+        ++sc;
+        tc_fence_after();
+        const bool diag = (j == qe);
+        // all 128 scores of the row in one TMEM load batch
+        uint32_t v[128];
 #pragma unroll
-      for (int e = 0; e < 64; e += 8) {
-#pragma unroll
-        for (int a = 0; a < 4; ++a) {
-          float x0 = __uint_as_float(v[e + 2 * a]), x1 = __uint_as_float(v[e + 2 * a + 1]);
-          if constexpr (kDiag) {
-            if (c0 + e + 2 * a > r) x0 = -INFINITY;
-            if (c0 + e + 2 * a + 1 > r) x1 = -INFINITY;
-          }
-          float t;
-          asm("max.f32 %0, %1, %2, %3;" : "=f"(t) : "f"(mx[a]), "f"(x0), "f"(x1));
-          mx[a] = t;
-        }
-      }
-      float pm;
-      asm("max.f32 %0, %1, %2, %3;" : "=f"(pm) : "f"(mx[0]), "f"(mx[1]), "f"(mx[2]));
-      pm = fmaxf(pm, mx[3]);
-      s.red[b][half][r] = pm;
-      mbar_arrive(&s.xchg[b]);
-      return true;
-    };
-    auto exp_tile = [&](auto diag_tag, const uint32_t (&v)[64], int b, float m_new) -> float {
-      constexpr bool kDiag = decltype(diag_tag)::value;
-      const float2 nm2 = make_float2(-m_new, -m_new);
-      float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint8_t* p_row = s.p[b] + half * (kTile * 128) + r * 128;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 8; e += 2) {
-          const int c = q * 8 + e;
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc2, nm2);
-          float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-          if constexpr (kDiag) {
-            if (c0 + c > r) p.x = 0.f;
-            if (c0 + c + 1 > r) p.y = 0.f;
-          }
-          rs[(e >> 1) & 1] = __fadd2_rn(rs[(e >> 1) & 1], p);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(p.x, p.y);
-          pk[e >> 1] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        *reinterpret_cast<uint4*>(p_row + ((q ^ sw) * 16)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      const float2 t = __fadd2_rn(rs[0], rs[1]);
-      return t.x + t.y;
-    };
-    auto update_o = [&](int pb, float corr) {
-      const uint32_t pv_addr = tmem + lane_off + kPVCol0 + (uint32_t)(pb * D + half * kHalfD);
-      uint32_t w[kHalfD];
-#pragma unroll
-      for (int c = 0; c < kHalfD / 32; ++c) tmem_ld32(pv_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&w[c * 32]));
-      tmem_wait_ld();
-      const float2 c2 = make_float2(corr, corr);
-#pragma unroll
-      for (int e = 0; e < kHalfD / 2; ++e)
-        o[e] = __ffma2_rn(o[e], c2, make_float2(__uint_as_float(w[2 * e]), __uint_as_float(w[2 * e + 1])));
-    };
-
-    for (int j = 0; j < n_kv; ++j) {
-      const int b = j & 1;
-      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-      const bool diag = (j0 + j == qt);
-      if (!warp_wait(&s.s_full[b], ph, &s.abort, 31)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t v[64];
-      {
-        const uint32_t s_addr = tmem + lane_off + kSCol0 + (uint32_t)(b * kTile + c0);
-        tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
-        tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
         tmem_wait_ld();
-      }
-      float corr_unused = 0.f;
-      if (diag) softmax_tile(std::true_type{}, v, b, corr_unused);
-      else softmax_tile(std::false_type{}, v, b, corr_unused);
-      if (!warp_wait(&s.xchg[b], ph, &s.abort, 32)) { ok = false; break; }
-      const float mx = fmaxf(s.red[b][0][r], s.red[b][1][r]);
-      const float m_new = fmaxf(m, mx * scale_log2);
-      const float corr = fast_exp2(m - m_new);
-      const float rs = diag ? exp_tile(std::true_type{}, v, b, m_new) : exp_tile(std::false_type{}, v, b, m_new);
-      fence_proxy_async_smem();
-      tc_fence_before();
-      mbar_arrive(&s.p_full[b]);
-      l = l * corr + rs;
-      // O(j-1) = O(j-2) * corr(j-1) + P(j-1).V(j-1), this thread's D/2 output columns
-      if (j >= 1) {
-        const int pb = (j - 1) & 1;
-        if (!warp_wait(&s.pv_full[pb], (uint32_t)((j - 1) >> 1) & 1u, &s.abort, 33)) { ok = false; break; }
-        tc_fence_after();
-        update_o(pb, corr_prev);
+        if (diag) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (c > r) v[c] = __float_as_uint(-INFINITY);
+        }
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 128; c += 8) {
+#pragma unroll
+          for (int a = 0; a < 4; ++a) {
+            float tm;
+            asm("max.f32 %0, %1, %2, %3;"
+                : "=f"(tm)
+                : "f"(mx[a]), "f"(__uint_as_float(v[c + 2 * a])), "f"(__uint_as_float(v[c + 2 * a + 1])));
+            mx[a] = tm;
+          }
+        }
+        float rmax;
+        asm("max.f32 %0, %1, %2, %3;" : "=f"(rmax) : "f"(mx[0]), "f"(mx[1]), "f"(mx[2]));
+        rmax = fmaxf(rmax, mx[3]) * scale_log2;
+        // lazy rescale: move the reference max only when it grew by more than 2^8
+        float factor = 1.f;
+        if (t == 0) {
+          m_ref = rmax;
+        } else if (rmax > m_ref + kRescaleLog2) {
+          factor = fast_exp2(m_ref - rmax);
+          m_ref = rmax;
+        }
+        if (__any_sync(0xffffffffu, factor != 1.f)) {
+          // O holds P.V of tiles < t, complete: S(t) was issued after them. Rescale in TMEM.
+#pragma unroll 1
+          for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the scores stay in registers
+            uint32_t w[16];
+            tmem_ld16(o_addr + c * 16, w);
+            tmem_wait_ld();
+#pragma unroll
+            for (int k2 = 0; k2 < 16; ++k2) w[k2] = __float_as_uint(__uint_as_float(w[k2]) * factor);
+            tmem_st16(o_addr + c * 16, w);
+          }
+          tmem_wait_st();
+        }
+        // P = exp2(s * scale_log2 - m_ref) as bf16 pairs, packed in place: the pair of
+        // keys (c, c+1) lands in v[c/2], a score already consumed (masked keys give 0)
+        const float2 nm2 = make_float2(-m_ref, -m_ref);
+        float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int c = 0; c < 128; c += 2) {
+          const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc2, nm2);
+          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          rs[(c >> 1) & 1] = __fadd2_rn(rs[(c >> 1) & 1], p);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(p.x, p.y);
+          v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
+        }
+        tmem_st32(s_addr, v);
+        tmem_st32(s_addr + 32, v + 32);
+        tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&s.pv_free[pb]);
+        mbar_arrive(&s.p_full[e]);
+        const float2 rsum = __fadd2_rn(rs[0], rs[1]);
+        l = l * factor + (rsum.x + rsum.y);
       }
-      corr_prev = corr;
-      m = m_new;
-    }
-    if (ok) {
-      const int pb = (n_kv - 1) & 1;
-      ok = warp_wait(&s.pv_full[pb], (uint32_t)((n_kv - 1) >> 1) & 1u, &s.abort, 34);
-      if (ok) {
-        tc_fence_after();
-        update_o(pb, corr_prev);
-        // total row sum = the two halves' partial sums (same running max)
-        const int fb = n_kv & 1;
-        s.red[fb][half][r] = l;
-        mbar_arrive(&s.xchg[fb]);
-        ok = warp_wait(&s.xchg[fb], (uint32_t)(n_kv >> 1) & 1u, &s.abort, 35);
-      }
-      const int fb = n_kv & 1;
-      float l_tot = 0.f;
-      if (ok) l_tot = s.red[fb][0][r] + s.red[fb][1][r];
-      bool write_out = ok;
-      int xi = n_kv + 1;  // next use of the xchg barriers (one phase per use, alternating slots)
-      if (ok && n_chunks > 1) {
-        // ---- split query tile: publish this chunk's partial, the last chunk combines
-        const int unit = (int)blockIdx.x;
-        float* st_m = reinterpret_cast<float*>(args.ws + args.ws_stats_off) + (size_t)unit * 2 * kTile;
-        float* o_part = reinterpret_cast<float*>(args.ws + args.ws_o_off) + (size_t)unit * kTile * D;
-        // layout [col/4][row][4]: a warp's 32 rows store 512 contiguous bytes per instruction
-        float4* op = reinterpret_cast<float4*>(o_part) + (size_t)(half * kHalfD / 4) * kTile + r;
+      if (!ok) break;
+      // ---------------- epilogue: O (complete after the unit's last P.V) -> output or partial
+      if (!warp_wait(&s.pv_done[e], dc & 1u, &s.abort, 33)) { ok = false; break; }
+      ++dc;
+      tc_fence_after();
+      bool write_out = true;
+      float linv = 1.0f / l;
+      if (un.n_chunks > 1) {
+        // Split query tile: publish this chunk's partial -- its running max, row sum and
+        // O / sum in fp16 (a weighted mean of V rows, rounded 2^-11 relative, far below
+        // the bf16 output's 2^-8) -- and let the chunk that finishes last combine.
+        const int slot = u * 2 + e;
+        float* st_m = reinterpret_cast<float*>(args.ws + args.ws_stats_off) + (size_t)slot * 2 * kTile;
+        uint4* op = reinterpret_cast<uint4*>(args.ws + args.ws_o_off) + (size_t)slot * (kTile * D / 8) + r;
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t w[32];
+          tmem_ld32(o_addr + c * 32, w);
+          tmem_wait_ld();
 #pragma unroll
-        for (int g = 0; g < kHalfD / 4; ++g)
-          op[(size_t)g * kTile] = make_float4(o[2 * g].x, o[2 * g].y, o[2 * g + 1].x, o[2 * g + 1].y);
-        if (half == 0) {
-          st_m[r] = m;
-          st_m[kTile + r] = l_tot;
+          for (int g = 0; g < 4; ++g) {  // layout [col/8][row][8]: a warp stores 512 contiguous bytes
+            uint32_t hv[4];
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+              __half2 h = __floats2half2_rn(__uint_as_float(w[8 * g + 2 * k2]) * linv,
+                                            __uint_as_float(w[8 * g + 2 * k2 + 1]) * linv);
+              hv[k2] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            op[(size_t)(c * 4 + g) * kTile] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          }
         }
+        tc_fence_before();
+        mbar_arrive(&s.o_free[e]);  // the next unit's first P.V may overwrite O_e
+        st_m[r] = m_ref;
+        st_m[kTile + r] = l;
         __threadfence();
-        int* counter = reinterpret_cast<int*>(args.ws) + head * args.q_tiles + qt;
-        const int sb = xi & 1;
-        mbar_arrive(&s.xchg[sb]);
-        ok = warp_wait(&s.xchg[sb], (uint32_t)(xi >> 1) & 1u, &s.abort, 36);
-        ++xi;
-        if (ok && threadIdx.x == 0) s.red[sb][0][0] = (float)atomicAdd(counter, 1);
-        if (ok) {
-          mbar_arrive(&s.xchg[xi & 1]);
-          ok = warp_wait(&s.xchg[xi & 1], (uint32_t)(xi >> 1) & 1u, &s.abort, 37);
-          ++xi;
-        }
-        write_out = ok && (int)s.red[sb][0][0] == n_chunks - 1;
+        mbar_arrive(&s.eng_sync[e]);
+        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 36)) { ok = false; break; }
+        ++xc;
+        int* counter = reinterpret_cast<int*>(args.ws) + un.head * q_tiles + qe;
+        if ((threadIdx.x & (kEngineThreads - 1)) == 0) s.flag[e] = atomicAdd(counter, 1);
+        mbar_arrive(&s.eng_sync[e]);
+        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 37)) { ok = false; break; }
+        ++xc;
+        int n_e = 0;  // chunks of this pair that cover keys of engine e's query tile
+        for (int c = 0; c < un.n_chunks; ++c)
+          if (c * args.chunk <= qe) ++n_e;
+        write_out = (s.flag[e] == n_e - 1);
         if (write_out) {
+          // Combine every chunk's partial, this one's included, read back in chunk order:
+          // the sum does not depend on which chunk finished last.
           __threadfence();
-          const int base_unit = (int)(blockIdx.x / (unsigned)heads) - chunk;  // unit index (per head) of chunk 0
           const float* ws_stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
-          const float* ws_o = reinterpret_cast<const float*>(args.ws + args.ws_o_off);
+          const uint4* ws_o = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
+          float mc[kMaxChunks], lc[kMaxChunks];
+          size_t sl[kMaxChunks];
           float mmax = -INFINITY;
-          for (int c = 0; c < n_chunks; ++c) {
-            const size_t uc = (size_t)(base_unit + c) * heads + head;
-            const float mc = (c == chunk) ? m : __ldcg(ws_stats + uc * 2 * kTile + r);
-            mmax = fmaxf(mmax, mc);
+#pragma unroll
+          for (int c = 0; c < kMaxChunks; ++c) {
+            sl[c] = (size_t)(((un.v0 + min(c, n_e - 1)) * heads + un.head) * 2 + e);
+            mc[c] = c < n_e ? __ldcg(ws_stats + sl[c] * 2 * kTile + r) : -INFINITY;
+            lc[c] = c < n_e ? __ldcg(ws_stats + sl[c] * 2 * kTile + kTile + r) : 0.f;
+            mmax = fmaxf(mmax, mc[c]);
           }
-          float2 acc[kHalfD / 2];
+          float wc[kMaxChunks], lsum = 0.f;
 #pragma unroll
-          for (int e = 0; e < kHalfD / 2; ++e) acc[e] = make_float2(0.f, 0.f);
-          float lsum = 0.f;
-          for (int c = 0; c < n_chunks; ++c) {
-            const size_t uc = (size_t)(base_unit + c) * heads + head;
-            float mc, lc;
-            if (c == chunk) {
-              mc = m;
-              lc = l_tot;
-            } else {
-              mc = __ldcg(ws_stats + uc * 2 * kTile + r);
-              lc = __ldcg(ws_stats + uc * 2 * kTile + kTile + r);
-            }
-            const float w = fast_exp2(mc - mmax);
-            lsum = fmaf(w, lc, lsum);
-            const float2 w2 = make_float2(w, w);
-            if (c == chunk) {
+          for (int c = 0; c < kMaxChunks; ++c) {
+            wc[c] = c < n_e ? fast_exp2(mc[c] - mmax) * lc[c] : 0.f;
+            lsum += wc[c];
+          }
+          const float inv = 1.0f / lsum;
+#pragma unroll 1
+          for (int cc = 0; cc < D / 32; ++cc) {
+            uint4 t[kMaxChunks][4];  // every chunk's 32 columns of this row, loads all in flight
 #pragma unroll
-              for (int e = 0; e < kHalfD / 2; ++e) acc[e] = __ffma2_rn(o[e], w2, acc[e]);
-            } else {
-              const float4* src =
-                  reinterpret_cast<const float4*>(ws_o + uc * kTile * D) + (size_t)(half * kHalfD / 4) * kTile + r;
+            for (int c = 0; c < kMaxChunks; ++c)
 #pragma unroll
-              for (int e = 0; e < kHalfD / 4; ++e) {
-                const float4 t = __ldcg(src + (size_t)e * kTile);
-                acc[2 * e] = __ffma2_rn(make_float2(t.x, t.y), w2, acc[2 * e]);
-                acc[2 * e + 1] = __ffma2_rn(make_float2(t.z, t.w), w2, acc[2 * e + 1]);
+              for (int g = 0; g < 4; ++g)
+                t[c][g] = c < n_e ? __ldcg(ws_o + sl[c] * (kTile * D / 8) + (size_t)(cc * 4 + g) * kTile + r)
+                                  : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+              float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+              for (int c = 0; c < kMaxChunks; ++c) {
+                const __half2* h = reinterpret_cast<const __half2*>(&t[c][g]);
+#pragma unroll
+                for (int k2 = 0; k2 < 4; ++k2) {
+                  const float2 x = __half22float2(h[k2]);
+                  f[2 * k2] = fmaf(x.x, wc[c], f[2 * k2]);
+                  f[2 * k2 + 1] = fmaf(x.y, wc[c], f[2 * k2 + 1]);
+                }
               }
+#pragma unroll
+              for (int k2 = 0; k2 < 8; ++k2) f[k2] *= inv;
+              const int c8 = cc * 4 + g;  // 16-byte chunk index within the output row
+              uint8_t* rowp = s.q[e] + (c8 / 8) * (kTile * 128) + r * 128;
+              *reinterpret_cast<uint4*>(rowp + (((c8 & 7) ^ sw) * 16)) = pack16<bf16>(f);
             }
           }
-#pragma unroll
-          for (int e = 0; e < kHalfD / 2; ++e) o[e] = acc[e];
-          l_tot = lsum;
-          if (threadIdx.x == 0) *counter = 0;  // ready for the next launch on this workspace
+          if ((threadIdx.x & (kEngineThreads - 1)) == 0) *counter = 0;  // ready for the next launch
         }
+      } else {
+        // stage the bf16 output tile in this engine's Q buffer (its MMAs are complete) in
+        // the 128-byte-swizzled layout of the output map
+#pragma unroll 1
+        for (int cc = 0; cc < D / 32; ++cc) {
+          uint32_t w[32];
+          tmem_ld32(o_addr + cc * 32, w);
+          tmem_wait_ld();
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            float f[8];
+#pragma unroll
+            for (int k2 = 0; k2 < 8; ++k2) f[k2] = __uint_as_float(w[q4 * 8 + k2]) * linv;
+            const int c8 = cc * 4 + q4;
+            uint8_t* rowp = s.q[e] + (c8 / 8) * (kTile * 128) + r * 128;
+            *reinterpret_cast<uint4*>(rowp + (((c8 & 7) ^ sw) * 16)) = pack16<bf16>(f);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s.o_free[e]);  // the next unit's first P.V may overwrite O_e
       }
       if (write_out) {
-        // Stage the bf16 output tile in the Q buffer (free: every MMA has completed) in
-        // the 128-byte-swizzled layout of the output tensor map, then one TMA store per
-        // 64-column sub-tile; rows past seq are clipped by the TMA unit.
-        const float linv = 1.0f / l_tot;
-        const int col0 = half * kHalfD;
-        uint8_t* orow = s.q + (col0 / 64) * (kTile * 128) + r * 128;
-#pragma unroll
-        for (int c = 0; c < kHalfD / 8; ++c) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            f[2 * e] = o[c * 4 + e].x * linv;
-            f[2 * e + 1] = o[c * 4 + e].y * linv;
-          }
-          const int ch = ((col0 % 64) / 8 + c) ^ sw;
-          *reinterpret_cast<uint4*>(orow + ch * 16) = pack16<bf16>(f);
-        }
+        // TMA store of the staged tile; rows past seq are clipped by the TMA unit
         fence_proxy_async_smem();
-        mbar_arrive(&s.xchg[xi & 1]);
-        const bool staged = warp_wait(&s.xchg[xi & 1], (uint32_t)(xi >> 1) & 1u, &s.abort, 38);
-        if (staged && threadIdx.x == 0) {
+        mbar_arrive(&s.eng_sync[e]);
+        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 38)) { ok = false; break; }
+        ++xc;
+        if ((threadIdx.x & (kEngineThreads - 1)) == 0) {
 #pragma unroll
-          for (int c = 0; c < kSub; ++c) tma_store_3d(&map_o, s.q + c * (kTile * 128), c * 64, q0, head);
+          for (int c = 0; c < kSub; ++c) tma_store_3d(&map_o, s.q[e] + c * (kTile * 128), c * 64, qe * kTile, un.head);
           tma_store_commit();
           tma_store_wait_read();
         }
       }
+      // the Q buffer may be refilled once the output staging has been read
+      if ((threadIdx.x & (kEngineThreads - 1)) == 0) mbar_arrive(&s.q_empty[e]);
     }
   }
 
@@ -699,31 +796,107 @@ int make_qkv_map(CUtensorMap* m, const void* base, int heads, int seq, int d, co
   return make_tensor_map_bf16(m, base, 3, dims, strides, box, what);
 }
 
-// Work decomposition shared by the workspace-size query and the launch.
-struct AttnPlan {
-  int q_tiles = 0, chunk = 0, units_per_head = 0;
-  size_t stats_off = 0, o_off = 0, ws_bytes = 0;  // ws_bytes == 0: no split, no workspace
-};
-
 inline size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 
-AttnPlan plan_attention(int heads, int seq, int d, bool split) {
+// Work decomposition and CTA schedule, shared by the workspace-size query and the launch.
+struct AttnPlan {
+  int q_tiles = 0, pairs = 0, chunk = 0, units = 0, ctas = 0;
+  size_t stats_off = 0, o_off = 0, ws_bytes = 0;  // ws_bytes == 0: no split, no workspace
+  std::vector<uint16_t> cta_off, unit_list;       // empty: round-robin over CTAs
+};
+
+// Cost of a unit in "engine tiles" (tensor-core and exp work scale with the key tiles
+// both engines process), plus a fixed charge for the unit's prologue and epilogue
+// and, when split, for publishing and combining partials.
+inline int unit_cost(const Unit& un, int q_tiles) {
+  int c = 3;
+  for (int e = 0; e < 2; ++e) {
+    const int qe = 2 * un.pm + e;
+    if (qe < q_tiles) c += std::max(0, std::min(un.n, qe + 1 - un.j0));
+  }
+  return c + (un.n_chunks > 1 ? 2 : 0);
+}
+
+// Longest-processing-time assignment of units to `ctas` CTAs; returns the makespan and
+// (optionally) fills the per-CTA lists.
+inline long lpt_schedule(int heads, int pairs, int q_tiles, int C, int units, int ctas, AttnPlan* out) {
+  std::vector<std::pair<int, int>> cost(units);  // (cost, unit)
+  for (int u = 0; u < units; ++u) cost[u] = {unit_cost(decode_unit(u, heads, pairs, q_tiles, C), q_tiles), u};
+  std::stable_sort(cost.begin(), cost.end(), [](const std::pair<int, int>& a, const std::pair<int, int>& b) {
+    return a.first > b.first;
+  });
+  std::vector<long> load(ctas, 0);
+  std::vector<std::vector<uint16_t>> lists(out ? ctas : 0);
+  for (const auto& cu : cost) {
+    int best = 0;
+    for (int b = 1; b < ctas; ++b)
+      if (load[b] < load[best]) best = b;
+    load[best] += cu.first;
+    if (out) lists[best].push_back((uint16_t)cu.second);
+  }
+  if (out) {
+    out->cta_off.assign(1, 0);
+    out->unit_list.clear();
+    for (int b = 0; b < ctas; ++b) {
+      out->unit_list.insert(out->unit_list.end(), lists[b].begin(), lists[b].end());
+      out->cta_off.push_back((uint16_t)out->unit_list.size());
+    }
+  }
+  return *std::max_element(load.begin(), load.end());
+}
+
+inline int count_units(int heads, int pairs, int q_tiles, int C) {
+  int per_head = 0;
+  for (int pm = 0; pm < pairs; ++pm) per_head += (pair_tiles(pm, q_tiles) + C - 1) / C;
+  return heads * per_head;
+}
+
+AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
   AttnPlan p;
   p.q_tiles = (seq + kTile - 1) / kTile;
-  p.chunk = p.q_tiles;
-  if (split) {
-    // halve the chunk until there are at least two units per SM (or chunks of 2 tiles)
-    const int target = 2 * sm_count();
-    while (p.chunk > 2 && heads * units_below(p.q_tiles, p.chunk) < target) p.chunk = (p.chunk + 1) / 2;
+  p.pairs = (p.q_tiles + 1) / 2;
+  const int max_nt = pair_tiles(p.pairs - 1, p.q_tiles);
+  // Candidate chunk sizes: the whole key range (no split), or any smaller chunk when a
+  // workspace is available and the units fit the schedule table.
+  long best_span = -1;
+  int best_c = max_nt;
+  const int min_c = (max_nt + kMaxChunks - 1) / kMaxChunks;
+  for (int C = max_nt; C >= min_c; --C) {
+    if (C < max_nt && !allow_split) break;
+    const int units = count_units(heads, p.pairs, p.q_tiles, C);
+    if (units > kMaxSched) {
+      if (C == max_nt) { best_c = C; best_span = -1; }
+      break;
+    }
+    const int ctas = std::min(units, sms);
+    const long span = lpt_schedule(heads, p.pairs, p.q_tiles, C, units, ctas, nullptr);
+    if (best_span < 0 || span < best_span) {
+      best_span = span;
+      best_c = C;
+    }
   }
-  p.units_per_head = units_below(p.q_tiles, p.chunk);
-  if (p.chunk < p.q_tiles) {
-    const size_t units = (size_t)heads * p.units_per_head;
+  p.chunk = best_c;
+  p.units = count_units(heads, p.pairs, p.q_tiles, p.chunk);
+  p.ctas = std::min(p.units, sms);
+  if (p.units <= kMaxSched && p.ctas <= kMaxCtas) lpt_schedule(heads, p.pairs, p.q_tiles, p.chunk, p.units, p.ctas, &p);
+  if (p.chunk < max_nt) {
     p.stats_off = round256((size_t)heads * p.q_tiles * sizeof(int));
-    p.o_off = p.stats_off + round256(units * 2 * kTile * sizeof(float));
-    p.ws_bytes = p.o_off + units * kTile * (size_t)d * sizeof(float);
+    p.o_off = p.stats_off + round256((size_t)p.units * 2 * 2 * kTile * sizeof(float));
+    p.ws_bytes = p.o_off + (size_t)p.units * 2 * kTile * (size_t)d * sizeof(__half);
   }
   return p;
+}
+
+// Plans are cached per (heads, seq, d, split, SMs); the LPT search costs a few ms.
+const AttnPlan& cached_plan(int heads, int seq, int d, bool allow_split) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, bool, int>, AttnPlan> cache;
+  const int sms = sm_count();
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_tuple(heads, seq, d, allow_split, sms);
+  auto it = cache.find(key);
+  if (it == cache.end()) it = cache.emplace(key, plan_attention(heads, seq, d, allow_split, sms)).first;
+  return it->second;
 }
 
 template <int D>
@@ -735,10 +908,9 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   if (!rc) rc = make_qkv_map(&mv, v, heads, seq, D, "nkl_attention(v)");
   if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, "nkl_attention(out)");
   if (rc) return rc;
-  AttnPlan plan = plan_attention(heads, seq, D, ws != nullptr);
-  if (ws != nullptr && plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
+  const AttnPlan& plan = cached_plan(heads, seq, D, ws != nullptr);
+  if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
     return fail(NKL_ERR_ARG, "nkl_attention_ws: workspace %zu B < required %zu B", ws_bytes, plan.ws_bytes);
-  if (plan.ws_bytes == 0) ws = nullptr;
   constexpr size_t smem = attn_smem_bytes<D>();
   static bool attr_set[64] = {false};
   int dev = 0;
@@ -749,18 +921,19 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
     if (dev >= 0 && dev < 64) attr_set[dev] = true;
   }
   AttnArgs a;
-  a.out = static_cast<bf16*>(out);
-  a.ws = static_cast<unsigned char*>(ws);
+  a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;
   a.heads = heads;
-  a.seq = seq;
   a.q_tiles = plan.q_tiles;
+  a.pairs = plan.pairs;
   a.chunk = plan.chunk;
-  a.units_per_head = plan.units_per_head;
+  a.units = plan.units;
   a.scale_log2 = scale * kLog2e;
   a.ws_stats_off = plan.stats_off;
   a.ws_o_off = plan.o_off;
-  const unsigned grid = (unsigned)(heads * plan.units_per_head);
-  attn_fwd_bf16_kernel<D><<<grid, kAttnThreads, smem, st>>>(mq, mk, mv, mo, a);
+  a.n_ctas_listed = plan.cta_off.empty() ? 0 : plan.ctas;
+  for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
+  for (size_t i = 0; i < plan.unit_list.size(); ++i) a.unit_list[i] = plan.unit_list[i];
+  attn_fwd_bf16_kernel<D><<<plan.ctas, kAttnThreads, smem, st>>>(mq, mk, mv, mo, a);
   return check_launch("nkl_attention");
 }
 
@@ -812,7 +985,7 @@ extern "C" int nkl_attention(const void* q, const void* k, const void* v, void* 
 extern "C" size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
   if (dtype != NKL_BFLOAT16 || heads <= 0 || seq <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
   if (heads > 65535 || seq > (1 << 24)) return 0;
-  return plan_attention((int)heads, (int)seq, (int)head_dim, true).ws_bytes;
+  return cached_plan((int)heads, (int)seq, (int)head_dim, true).ws_bytes;
 }
 
 extern "C" int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, void* workspace,
