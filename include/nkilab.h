@@ -148,11 +148,11 @@ size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64_t head_dim
 
 /* nkl_attention with a caller-owned workspace that lets the bf16 kernel split the
  * causal key range of long query tiles into chunks spread over all SMs (split-KV);
- * partial results are combined in a fixed chunk order, so the output is bit-identical
- * for any scheduling. The workspace (>= nkl_attention_workspace_size bytes, 256-byte
- * aligned) must be zero-filled before its first use; every call leaves it ready for
- * the next. Calls that overlap on the GPU must not share a workspace. NULL workspace
- * or fp32: same as nkl_attention.
+ * a second kernel on the same stream combines the partial results in a fixed chunk
+ * order, so the output is bit-identical for any scheduling. The workspace
+ * (>= nkl_attention_workspace_size bytes, 256-byte aligned) needs no initialisation.
+ * Calls that overlap on the GPU must not share a workspace. NULL workspace or fp32:
+ * same as nkl_attention.
  * Replaces nkilab/ops.py:77-91 (attention, any "flash*" variant)
  *   -> nkilab/kernels/attention.py:155-325. */
 int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, void* workspace,

@@ -14,22 +14,23 @@
 // running max grows by more than 2^8 (P values stay <= 256, exact in fp32 and
 // relatively exact in bf16), which gives the same softmax up to rounding.
 //
-// bf16 kernel (sm_100a): persistent, one CTA per SM, two softmax engines per CTA.
-//   work unit  (head, query-tile pair 2p / 2p+1, chunk of the causal key range); the
-//              host orders units longest first and assigns them to CTAs greedily
-//              (LPT); query tiles whose key range is split over several units write
-//              partial (O, max, sum) to a workspace and the chunk that finishes last
-//              combines them in chunk order (result independent of finish order)
-//   warps 0-3  engine 0 (query tile 2p), warps 4-7 engine 1 (tile 2p+1); thread =
-//              query row = TMEM lane. Per key tile: tcgen05.ld of the 128 scores, row
-//              max, lazy rescale of O in TMEM, exp2 with the scale folded into one FMA,
-//              P (bf16 pairs) written back over the score columns with tcgen05.st
-//   warp 8     TMA producer: Q of both engines per unit, K and V tiles through 2-deep
-//              rings shared by the engines
-//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer, interleaving the
-//              engines: S_e = Q_e K^T (smem x smem), O_e += P_e V (P from TMEM)
-//   TMEM       S/P of engine 0 [0,128), engine 1 [128,256), O_0 [256,256+d), O_1 after
-//   epilogue   O from TMEM, * 1/l, bf16, staged in the engine's Q buffer, TMA store
+// bf16 kernel (sm_100a): persistent, one CTA per SM.
+//   work unit  (head, query tile, chunk of its causal key range); the host orders units
+//              longest first and assigns them to CTAs greedily (LPT). A query tile whose
+//              key range is split over several units writes partial (O / sum, max, sum)
+//              to a workspace; a second kernel (programmatic dependent launch) merges
+//              the partials in chunk order, so the result does not depend on the schedule
+//   warps 0-7  softmax engine: two warps per TMEM lane quadrant, each taking 64 of the
+//              128 keys of every score row (row maxima and sums exchanged through shared
+//              memory). Per key tile: tcgen05.ld of the scores, row max, lazy rescale of
+//              O in TMEM, exp2 with the scale folded into one FMA, P (bf16 pairs)
+//              written back over the score columns with tcgen05.st
+//   warp 8     TMA producer: Q per unit (double buffered), K and V through 2-deep rings
+//   warp 9     TMEM allocator + single-thread tcgen05.mma issuer. S is double buffered
+//              in TMEM: S(t+2) = Q K(t+2)^T is issued right behind O += P(t) V(t), so the
+//              tensor core computes the next tile's scores while the engine exponentiates
+//   TMEM       S/P buffers [0,128) and [128,256), O [256, 256+d)
+//   epilogue   O from TMEM, * 1/l, bf16, staged in the unit's Q buffer, TMA store
 #include <algorithm>
 #include <map>
 #include <mutex>
@@ -51,10 +52,11 @@ __device__ unsigned int g_attn_dev_error = 0;
 using namespace sm100;
 
 constexpr int kTile = 128;  // query / key tile, as the reference's T (attention.py:24)
-constexpr int kEngineThreads = 128;
-constexpr int kAttnThreads = 2 * kEngineThreads + 64;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kEngineWarps = 8;  // two warps per TMEM lane quadrant, each taking half of every row
+constexpr int kEngineThreads = kEngineWarps * 32;
+constexpr int kProducerWarp = kEngineWarps;
+constexpr int kMmaWarp = kEngineWarps + 1;
+constexpr int kAttnThreads = kEngineThreads + 64;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 constexpr int kMaxCtas = 192;         // schedule table capacity (>= SMs of any sm_100 part)
@@ -65,6 +67,50 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Marks r[0..N) as defined here: placed after tcgen05.wait::ld, it keeps every use of
+// registers written by an asynchronous tcgen05.ld behind the wait that completes it.
+template <int N>
+__device__ __forceinline__ void reg_fence(uint32_t* r) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) asm volatile("" : "+r"(r[i]));
+}
+
+// Named barrier (ids 1..4) for the two engine warps that share a TMEM lane quadrant.
+__device__ __forceinline__ void pair_sync(int id) { asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory"); }
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float m;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(m) : "f"(a), "f"(b), "f"(c));
+  return m;
+}
+
+// Max of 64 fp32 scores held as bits.
+__device__ __forceinline__ float max64(const uint32_t* v) {
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int c = 0; c < 64; c += 8)
+#pragma unroll
+    for (int a = 0; a < 4; ++a) mx[a] = max3f(mx[a], __uint_as_float(v[c + 2 * a]), __uint_as_float(v[c + 2 * a + 1]));
+  return fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+}
+
+// P = 2^(s * scale_log2 - m) for the 64 scores in v[0..64), packed as bf16 pairs into
+// v[0..32) (pair (c, c+1) lands in v[c/2], a score already consumed); returns the fp32
+// sum of the 64 values.
+__device__ __forceinline__ float exp_pack64(uint32_t* v, float scale_log2, float neg_m) {
+  float rs0 = 0.f, rs1 = 0.f;
+#pragma unroll
+  for (int c = 0; c < 64; c += 2) {
+    const float p0 = fast_exp2(fmaf(__uint_as_float(v[c]), scale_log2, neg_m));
+    const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + 1]), scale_log2, neg_m));
+    rs0 += p0;
+    rs1 += p1;
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+    v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+  return rs0 + rs1;
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
@@ -82,18 +128,23 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
 template <int D>
 struct AttnSmem {
   static constexpr int kTileBytes = kTile * D * 2;
-  uint8_t q[2][kTileBytes];  // per engine: D/64 sub-tiles of [128 rows x 128 B]; output staging
+  uint8_t q[2][kTileBytes];  // Q double buffer: D/64 sub-tiles of [128 rows x 128 B]; output staging
   uint8_t k[2][kTileBytes];  // key ring, K-major (head_dim contiguous)
   uint8_t v[2][kTileBytes];  // value ring, N-major for the P.V product
   uint64_t q_full[2], q_empty[2];
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2], p_full[2], pv_done[2], o_free[2];
-  uint64_t eng_sync[2];  // engine-local barrier (128 arrivals) for the epilogue
+  uint64_t s_full[2];  // S(t) ready in TMEM buffer t & 1 (global tile count t)
+  uint64_t p_full[2];  // P(t) ready in buffer t & 1 (all engine threads)
+  uint64_t pv_step;    // one phase per P.V tile
+  uint64_t pv_done;    // one phase per unit: its last P.V complete
+  uint64_t o_free;     // engine has read O (all engine threads)
+  uint64_t eng_sync;   // output staging complete (all engine threads)
   uint64_t mma_done;
+  float xmax[2][2 * kTile];  // [tile parity][half * 128 + row]: row-max exchange
+  float xsum[2 * kTile];     // [half * 128 + row]: row-sum exchange
   uint32_t tmem_base;
   int abort;
-  int flag[2];
 };
 
 template <int D>
@@ -101,10 +152,10 @@ constexpr size_t attn_smem_bytes() {
   return sizeof(AttnSmem<D>);
 }
 
-// ---- split-KV work units over query-tile pairs
+// ---- split-KV work units
 struct AttnArgs {
   unsigned char* ws;  // NULL when no query tile is split
-  int heads, q_tiles, pairs, chunk, units;
+  int heads, q_tiles, chunk, units;
   float scale_log2;
   size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (max, sum) and O regions
   int n_ctas_listed;              // > 0: cta_off / unit_list give each CTA's units
@@ -113,33 +164,39 @@ struct AttnArgs {
 };
 
 struct Unit {
-  int head, pm, chunk, n_chunks, j0, n, v0;  // v0: per-head index of this pair's chunk 0
+  int head, qt, chunk, n_chunks, j0, n, v0;  // v0: per-head index of this query tile's chunk 0
 };
 
-__host__ __device__ __forceinline__ int pair_tiles(int pm, int q_tiles) {
-  return (2 * pm + 2 < q_tiles) ? 2 * pm + 2 : q_tiles;
-}
-
-// Unit index -> (head, pair, chunk). Units run head-fastest; pairs longest first; chunks ascending.
-__host__ __device__ __forceinline__ Unit decode_unit(int u, int heads, int pairs, int q_tiles, int C) {
+// Unit index -> (head, query tile, chunk). Units run head-fastest; query tiles longest
+// (latest) first; chunks of C key tiles ascending.
+__host__ __device__ __forceinline__ Unit decode_unit(int u, int heads, int q_tiles, int C) {
   Unit r;
   r.head = u % heads;
-  int v = u / heads, base = 0;
-  for (int pm = pairs - 1; pm >= 0; --pm) {
-    const int nt = pair_tiles(pm, q_tiles);
-    const int c = (nt + C - 1) / C;
+  const int v = u / heads;
+  if (C >= q_tiles) {  // no split: one unit per query tile
+    r.qt = q_tiles - 1 - v;
+    r.chunk = 0;
+    r.n_chunks = 1;
+    r.j0 = 0;
+    r.n = r.qt + 1;
+    r.v0 = v;
+    return r;
+  }
+  int base = 0;
+  for (int qt = q_tiles - 1; qt >= 0; --qt) {
+    const int c = (qt + C) / C;  // ceil((qt + 1) / C)
     if (v < base + c) {
-      r.pm = pm;
+      r.qt = qt;
       r.chunk = v - base;
       r.n_chunks = c;
       r.j0 = r.chunk * C;
-      r.n = (C < nt - r.j0) ? C : nt - r.j0;
+      r.n = (C < qt + 1 - r.j0) ? C : qt + 1 - r.j0;
       r.v0 = base;
       return r;
     }
     base += c;
   }
-  r.pm = -1;
+  r.qt = -1;
   return r;
 }
 
@@ -172,9 +229,12 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     if (threadIdx.x == 0) atomicCAS(&g_attn_dev_error, 0u, 40u);
     return;
   }
+  // The split-KV combine kernel, launched next with programmatic dependent launch, may be
+  // scheduled now; it waits in griddepcontrol.wait until this grid has completed.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   auto& s = *reinterpret_cast<AttnSmem<D>*>(smem_raw);
   constexpr uint32_t kTmemCols = 512;
-  constexpr uint32_t kOCol0 = 2 * kTile;  // O_e at 256 + e*D
+  constexpr uint32_t kOCol0 = 2 * kTile;  // S/P buffers at [0,128) and [128,256)
   constexpr uint32_t kIdescS = idesc_bf16_f32(kTile, kTile, false, false);
   constexpr uint32_t kIdescPV = idesc_bf16_f32(kTile, D, false, true);
   constexpr uint32_t kTileBytes = kTile * D * 2;
@@ -195,10 +255,11 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.p_full[i], kEngineThreads);
-      mbar_init(&s.pv_done[i], 1);
-      mbar_init(&s.o_free[i], kEngineThreads);
-      mbar_init(&s.eng_sync[i], kEngineThreads);
     }
+    mbar_init(&s.pv_step, 1);
+    mbar_init(&s.pv_done, 1);
+    mbar_init(&s.o_free, kEngineThreads);
+    mbar_init(&s.eng_sync, kEngineThreads);
     mbar_init(&s.mma_done, 1);
     s.abort = 0;
     fence_barrier_init();
@@ -218,62 +279,70 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   if (warp == kProducerWarp) {
     // ------------------------------------------------ TMA producer
     if (elect_one()) {
-      uint32_t kc = 0, vc = 0, qc[2] = {0, 0};
+      uint32_t kc = 0, vc = 0, qc = 0;
       int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1}, q_armed[2] = {-1, -1};
       bool ok = true;
       int u;
-      // Per unit: K/V tile 0 first (their slots free up as soon as the previous unit's
-      // MMAs consume them), then the engines' Q tiles (their buffers free up only after
-      // the previous unit's output has been staged and stored), then the remaining K/V.
-      auto load_kv = [&](const Unit& un, int t) -> bool {
-        const int j = un.j0 + t;
+      auto load_k = [&](const Unit& un, int t) -> bool {
         const int ks = kc & 1;
         if (!mbar_wait(&s.k_empty[ks], ((kc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 11)) return false;
         mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
         k_armed[ks] = (int)((kc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, j * kTile, un.head);
+          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, (un.j0 + t) * kTile, un.head);
         ++kc;
+        return true;
+      };
+      auto load_v = [&](const Unit& un, int t) -> bool {
         const int vs = vc & 1;
         if (!mbar_wait(&s.v_empty[vs], ((vc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 12)) return false;
         mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
         v_armed[vs] = (int)((vc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, j * kTile, un.head);
+          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, (un.j0 + t) * kTile, un.head);
         ++vc;
         return true;
       };
+      // Per unit, in the order the MMA warp consumes them: K(0), Q, K(1), then V(t)
+      // followed by K(t+2).
       for (int i = 0; ok && unit_of(args, i, u); ++i) {
-        const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
-        ok = load_kv(un, 0);
-        for (int e = 0; e < 2 && ok; ++e) {
-          const int qe = 2 * un.pm + e;
-          if (qe >= q_tiles || qe < un.j0) continue;  // engine has no query tile / no key in this unit
-          if (!mbar_wait(&s.q_empty[e], (qc[e] & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) { ok = false; break; }
-          mbar_arrive_expect_tx(&s.q_full[e], kTileBytes);
-          q_armed[e] = (int)(qc[e] & 1u);
+        const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
+        ok = load_k(un, 0);
+        if (ok) {
+          const int qb = qc & 1;
+          if (!mbar_wait(&s.q_empty[qb], ((qc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&s.q_full[qb], kTileBytes);
+          q_armed[qb] = (int)((qc >> 1) & 1u);
           for (int c = 0; c < kSub; ++c)
-            tma_load_3d(s.q[e] + c * (kTile * 128), &map_q, &s.q_full[e], c * 64, qe * kTile, un.head);
-          ++qc[e];
+            tma_load_3d(s.q[qb] + c * (kTile * 128), &map_q, &s.q_full[qb], c * 64, un.qt * kTile, un.head);
+          ++qc;
         }
-        for (int t = 1; t < un.n && ok; ++t) ok = load_kv(un, t);
+        if (ok && un.n > 1) ok = load_k(un, 1);
+        for (int t = 0; ok && t < un.n; ++t) {
+          ok = load_v(un, t);
+          if (ok && t + 2 < un.n) ok = load_k(un, t + 2);
+        }
       }
       if (!ok) {  // let issued copies land before shared memory is released
         const uint64_t t0 = globaltimer();
-        for (int e = 0; e < 2; ++e) {
-          if (q_armed[e] >= 0)
-            while (!mbar_try_wait(&s.q_full[e], (uint32_t)q_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-          if (k_armed[e] >= 0)
-            while (!mbar_try_wait(&s.k_full[e], (uint32_t)k_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-          if (v_armed[e] >= 0)
-            while (!mbar_try_wait(&s.v_full[e], (uint32_t)v_armed[e]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+        for (int b = 0; b < 2; ++b) {
+          if (q_armed[b] >= 0)
+            while (!mbar_try_wait(&s.q_full[b], (uint32_t)q_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+          if (k_armed[b] >= 0)
+            while (!mbar_try_wait(&s.k_full[b], (uint32_t)k_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+          if (v_armed[b] >= 0)
+            while (!mbar_try_wait(&s.v_full[b], (uint32_t)v_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
         }
       }
     }
+    __syncwarp();  // the warp reconverges here: the CTA barrier below must see all 32 lanes
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (elect_one()) {
-      uint32_t kc = 0, vc = 0, qc[2] = {0, 0}, pc[2] = {0, 0}, oc[2] = {0, 0};
+      uint32_t kc = 0, vc = 0, qc = 0, gt = 0, uc = 0;
       const uint64_t q_desc0 = smem_desc_sw128(smem_u32(s.q[0]), 16, 1024);
       const uint64_t q_desc1 = smem_desc_sw128(smem_u32(s.q[1]), 16, 1024);
       const uint64_t k_desc0 = smem_desc_sw128(smem_u32(s.k[0]), 16, 1024);
@@ -281,320 +350,210 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       const uint64_t v_desc0 = smem_desc_sw128(smem_u32(s.v[0]), kTile * 128, 1024);
       const uint64_t v_desc1 = smem_desc_sw128(smem_u32(s.v[1]), kTile * 128, 1024);
       bool ok = true;
-      // S_e = Q_e K^T for the K stage ks
-      auto issue_s = [&](int e, int ks) {
-        const uint64_t qd = e ? q_desc1 : q_desc0;
+      // S into TMEM buffer b from Q buffer qb and K stage ks
+      auto issue_s = [&](int qb, int ks, int b) {
+        const uint64_t qd = qb ? q_desc1 : q_desc0;
         const uint64_t kd = ks ? k_desc1 : k_desc0;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(((kk >> 2) * (kTile * 128) + (kk & 3) * 32) >> 4);
-          mma_bf16_ss(tmem + (uint32_t)(e * kTile), qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
+          mma_bf16_ss(tmem + (uint32_t)(b * kTile), qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
         }
-        mma_commit(&s.s_full[e]);
+        mma_commit(&s.s_full[b]);
       };
       int u;
       for (int i = 0; ok && unit_of(args, i, u); ++i) {
-        const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
-        int na[2];  // key tiles of this unit each engine takes part in
-        for (int e = 0; e < 2; ++e) {
-          const int qe = 2 * un.pm + e;
-          na[e] = (qe >= q_tiles) ? 0 : max(0, min(un.n, qe + 1 - un.j0));
+        const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
+        const int n = un.n;
+        const int qb = qc & 1;
+        if (!mbar_wait(&s.q_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
+        ++qc;
+        for (int t = 0; t < n && t < 2; ++t) {  // S for the unit's first two key tiles
+          const uint32_t ki = kc + (uint32_t)t;
+          if (!mbar_wait(&s.k_full[ki & 1], (ki >> 1) & 1u, &s.abort, &g_attn_dev_error, 21)) { ok = false; break; }
+          tc_fence_after();
+          issue_s(qb, ki & 1, (gt + t) & 1);
+          mma_commit(&s.k_empty[ki & 1]);
         }
-        for (int e = 0; e < 2 && ok; ++e) {
-          if (!na[e]) continue;
-          ok = mbar_wait(&s.q_full[e], qc[e] & 1u, &s.abort, &g_attn_dev_error, 20);
-          ++qc[e];
+        for (int t = 0; ok && t < n; ++t) {
+          const uint32_t G = gt + (uint32_t)t;
+          const int b = G & 1;
+          if (!mbar_wait(&s.p_full[b], (G >> 1) & 1u, &s.abort, &g_attn_dev_error, 22)) { ok = false; break; }
+          if (t == 0 && !mbar_wait(&s.o_free, (uc & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 23)) {
+            ok = false;
+            break;
+          }
+          const uint32_t vi = vc + (uint32_t)t;
+          if (!mbar_wait(&s.v_full[vi & 1], (vi >> 1) & 1u, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t vd = (vi & 1) ? v_desc1 : v_desc0;
+#pragma unroll
+          for (int kk = 0; kk < kTile / 16; ++kk)
+            mma_bf16_ts(tmem + kOCol0, tmem + (uint32_t)(b * kTile + kk * 8), vd + (uint32_t)(kk * 128), kIdescPV,
+                        (t > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(&s.pv_step);
+          mma_commit(&s.v_empty[vi & 1]);
+          if (t + 2 < n) {  // next-but-one S into this buffer, behind the P.V that reads its P
+            const uint32_t ki = kc + (uint32_t)t + 2;
+            if (!mbar_wait(&s.k_full[ki & 1], (ki >> 1) & 1u, &s.abort, &g_attn_dev_error, 25)) { ok = false; break; }
+            tc_fence_after();
+            issue_s(qb, ki & 1, b);
+            mma_commit(&s.k_empty[ki & 1]);
+          }
         }
         if (!ok) break;
-        // S for tile 0
-        {
-          const int ks = kc & 1;
-          if (!mbar_wait(&s.k_full[ks], (kc >> 1) & 1u, &s.abort, &g_attn_dev_error, 21)) break;
-          tc_fence_after();
-          for (int e = 0; e < 2; ++e)
-            if (na[e] > 0) issue_s(e, ks);
-          mma_commit(&s.k_empty[ks]);
-        }
-        for (int t = 0; t < un.n && ok; ++t) {
-          const uint32_t kn = kc + (uint32_t)t + 1;  // ring index of the next K tile
-          const uint32_t vi = vc + (uint32_t)t;
-          const int vs = vi & 1;
-          bool v_ready = false, k_ready = false;
-          for (int e = 0; e < 2 && ok; ++e) {
-            if (t >= na[e]) continue;
-            if (!mbar_wait(&s.p_full[e], pc[e] & 1u, &s.abort, &g_attn_dev_error, 22)) { ok = false; break; }
-            ++pc[e];
-            if (t == 0 && !mbar_wait(&s.o_free[e], (oc[e] & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 23)) {
-              ok = false;
-              break;
-            }
-            if (!v_ready) {
-              if (!mbar_wait(&s.v_full[vs], (vi >> 1) & 1u, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
-              v_ready = true;
-            }
-            tc_fence_after();
-            const uint64_t vd = vs ? v_desc1 : v_desc0;
-            const uint32_t p_tmem = tmem + (uint32_t)(e * kTile);
-#pragma unroll
-            for (int kk = 0; kk < kTile / 16; ++kk)
-              mma_bf16_ts(tmem + kOCol0 + (uint32_t)(e * D), p_tmem + (uint32_t)(kk * 8), vd + (uint32_t)(kk * 128),
-                          kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
-            if (t == na[e] - 1) {
-              mma_commit(&s.pv_done[e]);
-              ++oc[e];
-            }
-            if (t + 1 < na[e]) {  // next S of this engine, right behind its P.V (S/P columns reused)
-              if (!k_ready) {
-                if (!mbar_wait(&s.k_full[kn & 1], (kn >> 1) & 1u, &s.abort, &g_attn_dev_error, 25)) {
-                  ok = false;
-                  break;
-                }
-                k_ready = true;
-                tc_fence_after();
-              }
-              issue_s(e, kn & 1);
-            }
-          }
-          if (!ok) break;
-          mma_commit(&s.v_empty[vs]);
-          if (k_ready) mma_commit(&s.k_empty[kn & 1]);
-        }
-        kc += (uint32_t)un.n;
-        vc += (uint32_t)un.n;
+        mma_commit(&s.pv_done);
+        kc += (uint32_t)n;
+        vc += (uint32_t)n;
+        gt += (uint32_t)n;
+        ++uc;
       }
       // Every MMA issued by this thread has completed once mma_done flips.
       mma_commit(&s.mma_done);
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(&s.mma_done, 0) && globaltimer() - t0 < kWaitTimeoutNs) {}
     }
+    __syncwarp();  // the other lanes wait for the issuing lane before the CTA barrier and dealloc
   } else {
-    // ------------------------------------------------ softmax engines (warps 0-3, 4-7)
-    const int e = warp >> 2;
-    const int r = (warp & 3) * 32 + lane;  // query row within the tile == TMEM lane
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + (uint32_t)(e * kTile);
-    const uint32_t o_addr = tmem + lane_off + kOCol0 + (uint32_t)(e * D);
+    // ------------------------------------------------ softmax engine (warps 0-7)
+    // Warps w and w+4 share TMEM lane quadrant w: warp half hf takes keys hf*64 ..
+    // hf*64+63 of every S tile and O columns hf*D/2 .. hf*D/2+D/2-1 in the epilogue.
+    // Row maxima (per tile) and row sums (per unit) are exchanged through shared memory
+    // under a named barrier of the pair.
+    const int qd = warp & 3;
+    const int hf = warp >> 2;
+    const int r = qd * 32 + lane;  // query row within the tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    const uint32_t o_addr = tmem + lane_off + kOCol0 + (uint32_t)(hf * (D / 2));
+    const int pair_id = 1 + qd;
     const int sw = r & 7;
-    const float2 sc2 = make_float2(scale_log2, scale_log2);
-    uint32_t sc = 0, dc = 0, xc = 0;
+    const bool lead = threadIdx.x == 0;  // issues the output stores and frees the Q buffer
+    uint32_t gt = 0, uc = 0, xc = 0;
     bool ok = true;
     int u;
     for (int i = 0; ok && unit_of(args, i, u); ++i) {
-      const Unit un = decode_unit(u, heads, args.pairs, q_tiles, args.chunk);
-      const int qe = 2 * un.pm + e;
-      const int na = (qe >= q_tiles) ? 0 : max(0, min(un.n, qe + 1 - un.j0));
-      if (na == 0) continue;
-      float m_ref = -INFINITY, l = 0.f;
-      for (int t = 0; t < na; ++t) {
-        const int j = un.j0 + t;
-        if (!warp_wait(&s.s_full[e], sc & 1u, &s.abort, 31)) { ok = false; break; }
-        ++sc;
+      const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
+      const int qt = un.qt;
+      float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
+      for (int t = 0; t < un.n; ++t) {
+        const uint32_t G = gt + (uint32_t)t;
+        const int b = G & 1;
+        if (!warp_wait(&s.s_full[b], (G >> 1) & 1u, &s.abort, 31)) { ok = false; break; }
         tc_fence_after();
-        const bool diag = (j == qe);
-        // all 128 scores of the row in one TMEM load batch
-        uint32_t v[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(s_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+        uint32_t v[64];
+        const uint32_t s_addr = tmem + lane_off + (uint32_t)(b * kTile + hf * 64);
+        tmem_ld32(s_addr, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(s_addr + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
-        if (diag) {
+        reg_fence<64>(v);
+        if (un.j0 + t == qt) {  // diagonal tile: keys above the diagonal are masked
+          const int lim = r - hf * 64;
 #pragma unroll
-          for (int c = 0; c < 128; ++c)
-            if (c > r) v[c] = __float_as_uint(-INFINITY);
+          for (int c = 0; c < 64; ++c)
+            if (c > lim) v[c] = __float_as_uint(-INFINITY);
         }
-        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-        for (int c = 0; c < 128; c += 8) {
-#pragma unroll
-          for (int a = 0; a < 4; ++a) {
-            float tm;
-            asm("max.f32 %0, %1, %2, %3;"
-                : "=f"(tm)
-                : "f"(mx[a]), "f"(__uint_as_float(v[c + 2 * a])), "f"(__uint_as_float(v[c + 2 * a + 1])));
-            mx[a] = tm;
-          }
-        }
-        float rmax;
-        asm("max.f32 %0, %1, %2, %3;" : "=f"(rmax) : "f"(mx[0]), "f"(mx[1]), "f"(mx[2]));
-        rmax = fmaxf(rmax, mx[3]) * scale_log2;
-        // lazy rescale: move the reference max only when it grew by more than 2^8
+        // Row max over both halves. The pair barrier also guarantees that the partner
+        // has read its scores before this warp's P overwrites columns 32..63.
+        float* xm = s.xmax[b];
+        xm[hf * kTile + r] = max64(v);
+        pair_sync(pair_id);
+        const float mx = fmaxf(xm[r], xm[kTile + r]) * scale_log2;
+        // Exponents are taken against the reference max m_ref, which moves only when
+        // the row max grows by more than 2^8; O and l are then scaled by the factor.
         float factor = 1.f;
         if (t == 0) {
-          m_ref = rmax;
-        } else if (rmax > m_ref + kRescaleLog2) {
-          factor = fast_exp2(m_ref - rmax);
-          m_ref = rmax;
+          m_ref = mx;  // key 0 of the first tile is never masked: mx is finite
+        } else if (mx > m_ref + kRescaleLog2) {
+          factor = fast_exp2(m_ref - mx);
+          m_ref = mx;
         }
-        if (__any_sync(0xffffffffu, factor != 1.f)) {
-          // O holds P.V of tiles < t, complete: S(t) was issued after them. Rescale in TMEM.
+        if (t > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+          // O must hold P.V of every tile before this one: wait for P.V(G-1), the one
+          // that may still be running (P.V(G-2) completed before S(G) was computed).
+          if (!warp_wait(&s.pv_step, (G - 1) & 1u, &s.abort, 32)) { ok = false; break; }
+          tc_fence_after();
 #pragma unroll 1
-          for (int c = 0; c < D / 16; ++c) {  // 16 columns at a time: the scores stay in registers
+          for (int c = 0; c < D / 32; ++c) {  // this half's D/2 columns, 16 at a time
             uint32_t w[16];
             tmem_ld16(o_addr + c * 16, w);
             tmem_wait_ld();
+            reg_fence<16>(w);
 #pragma unroll
             for (int k2 = 0; k2 < 16; ++k2) w[k2] = __float_as_uint(__uint_as_float(w[k2]) * factor);
             tmem_st16(o_addr + c * 16, w);
           }
-          tmem_wait_st();
         }
-        // P = exp2(s * scale_log2 - m_ref) as bf16 pairs, packed in place: the pair of
-        // keys (c, c+1) lands in v[c/2], a score already consumed (masked keys give 0)
-        const float2 nm2 = make_float2(-m_ref, -m_ref);
-        float2 rs[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-#pragma unroll
-        for (int c = 0; c < 128; c += 2) {
-          const float2 x = __ffma2_rn(make_float2(__uint_as_float(v[c]), __uint_as_float(v[c + 1])), sc2, nm2);
-          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-          rs[(c >> 1) & 1] = __fadd2_rn(rs[(c >> 1) & 1], p);
-          __nv_bfloat162 h2 = __floats2bfloat162_rn(p.x, p.y);
-          v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
-        }
-        tmem_st32(s_addr, v);
-        tmem_st32(s_addr + 32, v + 32);
+        const float rs = exp_pack64(v, scale_log2, -m_ref);
+        tmem_st32(tmem + lane_off + (uint32_t)(b * kTile + hf * 32), v);  // P: bf16 pairs of this half's keys
         tmem_wait_st();
         tc_fence_before();
-        mbar_arrive(&s.p_full[e]);
-        const float2 rsum = __fadd2_rn(rs[0], rs[1]);
-        l = l * factor + (rsum.x + rsum.y);
+        mbar_arrive(&s.p_full[b]);
+        l = l * factor + rs;
       }
       if (!ok) break;
       // ---------------- epilogue: O (complete after the unit's last P.V) -> output or partial
-      if (!warp_wait(&s.pv_done[e], dc & 1u, &s.abort, 33)) { ok = false; break; }
-      ++dc;
+      if (!warp_wait(&s.pv_done, uc & 1u, &s.abort, 33)) { ok = false; break; }
       tc_fence_after();
-      bool write_out = true;
-      float linv = 1.0f / l;
+      uint32_t w[D / 2];  // this half's O columns, one TMEM load batch
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&w[c * 32]));
+      tmem_wait_ld();
+      reg_fence<D / 2>(w);
+      tc_fence_before();
+      mbar_arrive(&s.o_free);  // the next unit's first P.V may overwrite O
+      s.xsum[hf * kTile + r] = l;
+      pair_sync(pair_id);
+      const float lt = s.xsum[r] + s.xsum[kTile + r];
+      const float linv = 1.0f / lt;
+      const int qb = uc & 1;  // this unit's Q buffer
       if (un.n_chunks > 1) {
-        // Split query tile: publish this chunk's partial -- its running max, row sum and
-        // O / sum in fp16 (a weighted mean of V rows, rounded 2^-11 relative, far below
-        // the bf16 output's 2^-8) -- and let the chunk that finishes last combine.
-        const int slot = u * 2 + e;
-        float* st_m = reinterpret_cast<float*>(args.ws + args.ws_stats_off) + (size_t)slot * 2 * kTile;
-        uint4* op = reinterpret_cast<uint4*>(args.ws + args.ws_o_off) + (size_t)slot * (kTile * D / 8) + r;
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t w[32];
-          tmem_ld32(o_addr + c * 32, w);
-          tmem_wait_ld();
+        // Split query tile: this chunk's O / sum in fp16 (a weighted mean of V rows,
+        // rounded 2^-11 relative, far below the bf16 output's 2^-8) and its (max, sum);
+        // attn_combine_bf16_kernel merges the chunks once this kernel has completed.
+        uint4* op = reinterpret_cast<uint4*>(args.ws + args.ws_o_off) + (size_t)u * (kTile * D / 8) + r;
 #pragma unroll
-          for (int g = 0; g < 4; ++g) {  // layout [col/8][row][8]: a warp stores 512 contiguous bytes
-            uint32_t hv[4];
+        for (int g2 = 0; g2 < D / 16; ++g2) {  // layout [col/8][row][8]: a warp stores 512 contiguous bytes
+          uint32_t hv[4];
 #pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-              __half2 h = __floats2half2_rn(__uint_as_float(w[8 * g + 2 * k2]) * linv,
-                                            __uint_as_float(w[8 * g + 2 * k2 + 1]) * linv);
-              hv[k2] = *reinterpret_cast<uint32_t*>(&h);
-            }
-            op[(size_t)(c * 4 + g) * kTile] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+          for (int k2 = 0; k2 < 4; ++k2) {
+            __half2 h2 = __floats2half2_rn(__uint_as_float(w[8 * g2 + 2 * k2]) * linv,
+                                           __uint_as_float(w[8 * g2 + 2 * k2 + 1]) * linv);
+            hv[k2] = *reinterpret_cast<uint32_t*>(&h2);
           }
+          op[(size_t)(hf * (D / 16) + g2) * kTile] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
         }
-        tc_fence_before();
-        mbar_arrive(&s.o_free[e]);  // the next unit's first P.V may overwrite O_e
-        st_m[r] = m_ref;
-        st_m[kTile + r] = l;
-        __threadfence();
-        mbar_arrive(&s.eng_sync[e]);
-        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 36)) { ok = false; break; }
-        ++xc;
-        int* counter = reinterpret_cast<int*>(args.ws) + un.head * q_tiles + qe;
-        if ((threadIdx.x & (kEngineThreads - 1)) == 0) s.flag[e] = atomicAdd(counter, 1);
-        mbar_arrive(&s.eng_sync[e]);
-        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 37)) { ok = false; break; }
-        ++xc;
-        int n_e = 0;  // chunks of this pair that cover keys of engine e's query tile
-        for (int c = 0; c < un.n_chunks; ++c)
-          if (c * args.chunk <= qe) ++n_e;
-        write_out = (s.flag[e] == n_e - 1);
-        if (write_out) {
-          // Combine every chunk's partial, this one's included, read back in chunk order:
-          // the sum does not depend on which chunk finished last.
-          __threadfence();
-          const float* ws_stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
-          const uint4* ws_o = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
-          float mc[kMaxChunks], lc[kMaxChunks];
-          size_t sl[kMaxChunks];
-          float mmax = -INFINITY;
-#pragma unroll
-          for (int c = 0; c < kMaxChunks; ++c) {
-            sl[c] = (size_t)(((un.v0 + min(c, n_e - 1)) * heads + un.head) * 2 + e);
-            mc[c] = c < n_e ? __ldcg(ws_stats + sl[c] * 2 * kTile + r) : -INFINITY;
-            lc[c] = c < n_e ? __ldcg(ws_stats + sl[c] * 2 * kTile + kTile + r) : 0.f;
-            mmax = fmaxf(mmax, mc[c]);
-          }
-          float wc[kMaxChunks], lsum = 0.f;
-#pragma unroll
-          for (int c = 0; c < kMaxChunks; ++c) {
-            wc[c] = c < n_e ? fast_exp2(mc[c] - mmax) * lc[c] : 0.f;
-            lsum += wc[c];
-          }
-          const float inv = 1.0f / lsum;
-#pragma unroll 1
-          for (int cc = 0; cc < D / 32; ++cc) {
-            uint4 t[kMaxChunks][4];  // every chunk's 32 columns of this row, loads all in flight
-#pragma unroll
-            for (int c = 0; c < kMaxChunks; ++c)
-#pragma unroll
-              for (int g = 0; g < 4; ++g)
-                t[c][g] = c < n_e ? __ldcg(ws_o + sl[c] * (kTile * D / 8) + (size_t)(cc * 4 + g) * kTile + r)
-                                  : make_uint4(0u, 0u, 0u, 0u);
-#pragma unroll
-            for (int g = 0; g < 4; ++g) {
-              float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-              for (int c = 0; c < kMaxChunks; ++c) {
-                const __half2* h = reinterpret_cast<const __half2*>(&t[c][g]);
-#pragma unroll
-                for (int k2 = 0; k2 < 4; ++k2) {
-                  const float2 x = __half22float2(h[k2]);
-                  f[2 * k2] = fmaf(x.x, wc[c], f[2 * k2]);
-                  f[2 * k2 + 1] = fmaf(x.y, wc[c], f[2 * k2 + 1]);
-                }
-              }
-#pragma unroll
-              for (int k2 = 0; k2 < 8; ++k2) f[k2] *= inv;
-              const int c8 = cc * 4 + g;  // 16-byte chunk index within the output row
-              uint8_t* rowp = s.q[e] + (c8 / 8) * (kTile * 128) + r * 128;
-              *reinterpret_cast<uint4*>(rowp + (((c8 & 7) ^ sw) * 16)) = pack16<bf16>(f);
-            }
-          }
-          if ((threadIdx.x & (kEngineThreads - 1)) == 0) *counter = 0;  // ready for the next launch
+        if (hf == 0) {
+          float* st = reinterpret_cast<float*>(args.ws + args.ws_stats_off) + (size_t)u * 2 * kTile;
+          st[r] = m_ref;
+          st[kTile + r] = lt;
         }
       } else {
-        // stage the bf16 output tile in this engine's Q buffer (its MMAs are complete) in
-        // the 128-byte-swizzled layout of the output map
-#pragma unroll 1
-        for (int cc = 0; cc < D / 32; ++cc) {
-          uint32_t w[32];
-          tmem_ld32(o_addr + cc * 32, w);
-          tmem_wait_ld();
+        // Stage the bf16 output tile in the unit's Q buffer (its MMAs are complete) in the
+        // 128-byte-swizzled layout of the output map; then one TMA store per 64 columns.
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            float f[8];
+        for (int g2 = 0; g2 < D / 16; ++g2) {
+          const int g = hf * (D / 16) + g2;  // 16-byte chunk of the output row
+          float f[8];
 #pragma unroll
-            for (int k2 = 0; k2 < 8; ++k2) f[k2] = __uint_as_float(w[q4 * 8 + k2]) * linv;
-            const int c8 = cc * 4 + q4;
-            uint8_t* rowp = s.q[e] + (c8 / 8) * (kTile * 128) + r * 128;
-            *reinterpret_cast<uint4*>(rowp + (((c8 & 7) ^ sw) * 16)) = pack16<bf16>(f);
-          }
+          for (int k2 = 0; k2 < 8; ++k2) f[k2] = __uint_as_float(w[8 * g2 + k2]) * linv;
+          uint8_t* rowp = s.q[qb] + (g / 8) * (kTile * 128) + r * 128;
+          *reinterpret_cast<uint4*>(rowp + (((g & 7) ^ sw) * 16)) = pack16<bf16>(f);
         }
-        tc_fence_before();
-        mbar_arrive(&s.o_free[e]);  // the next unit's first P.V may overwrite O_e
-      }
-      if (write_out) {
-        // TMA store of the staged tile; rows past seq are clipped by the TMA unit
         fence_proxy_async_smem();
-        mbar_arrive(&s.eng_sync[e]);
-        if (!warp_wait(&s.eng_sync[e], xc & 1u, &s.abort, 38)) { ok = false; break; }
+        mbar_arrive(&s.eng_sync);
+        if (!warp_wait(&s.eng_sync, xc & 1u, &s.abort, 38)) { ok = false; break; }
         ++xc;
-        if ((threadIdx.x & (kEngineThreads - 1)) == 0) {
+        if (lead) {  // rows past seq are clipped by the TMA unit
 #pragma unroll
-          for (int c = 0; c < kSub; ++c) tma_store_3d(&map_o, s.q[e] + c * (kTile * 128), c * 64, qe * kTile, un.head);
+          for (int c = 0; c < kSub; ++c) tma_store_3d(&map_o, s.q[qb] + c * (kTile * 128), c * 64, qt * kTile, un.head);
           tma_store_commit();
           tma_store_wait_read();
         }
       }
       // the Q buffer may be refilled once the output staging has been read
-      if ((threadIdx.x & (kEngineThreads - 1)) == 0) mbar_arrive(&s.q_empty[e]);
+      if (lead) mbar_arrive(&s.q_empty[qb]);
+      gt += (uint32_t)un.n;
+      ++uc;
     }
   }
 
@@ -603,6 +562,83 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ split-KV combine
+// A query tile whose key range was split over n_e units has n_e partials: (m_c, l_c) per
+// row and O_c / l_c in fp16. The output row is sum_c w_c (O_c / l_c) / sum_c w_c with
+// w_c = 2^(m_c - max m) l_c, summed in chunk order so the result does not depend on the
+// schedule. One CTA of 64 threads covers 64 rows x 32 columns of one (job, head); every
+// partial's loads for a thread are issued together.
+
+constexpr int kMaxCombineJobs = 1024;
+
+struct CombineJob {
+  uint16_t qt, v0;  // query tile; per-head index of its chunk-0 unit
+  uint16_t n_e, pad;  // chunks covering the tile
+};
+
+struct CombineArgs {
+  const unsigned char* ws;
+  bf16* out;
+  int heads, seq, n_jobs;
+  size_t ws_stats_off, ws_o_off;
+  CombineJob job[kMaxCombineJobs];
+};
+
+template <int D>
+__global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_constant__ CombineArgs args) {
+  pdl_enter();  // the attention grid before this one has completed and its partials are visible
+  const CombineJob jb = args.job[blockIdx.x];
+  const int head = blockIdx.y;
+  const int r = (blockIdx.z & 1) * 64 + threadIdx.x;  // row within the query tile
+  const int g0 = (blockIdx.z >> 1) * 4;                // first 8-column group of the slice
+  const int row = jb.qt * kTile + r;
+  if (row >= args.seq) return;
+  const size_t stride = (size_t)args.heads;  // unit step between consecutive chunks
+  const size_t slot0 = (size_t)jb.v0 * args.heads + head;
+  const float* stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
+  const uint4* po = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
+  uint4 t[kMaxChunks][4];
+  float mc[kMaxChunks], lc[kMaxChunks];
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    const bool in = c < jb.n_e;
+    const size_t sl = slot0 + (size_t)(in ? c : 0) * stride;
+    mc[c] = in ? __ldcg(stats + sl * 2 * kTile + r) : -INFINITY;
+    lc[c] = in ? __ldcg(stats + sl * 2 * kTile + kTile + r) : 0.f;
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      t[c][g] = in ? __ldcg(po + sl * (kTile * D / 8) + (size_t)(g0 + g) * kTile + r) : make_uint4(0u, 0u, 0u, 0u);
+  }
+  float mmax = -INFINITY;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) mmax = fmaxf(mmax, mc[c]);
+  float wc[kMaxChunks], lsum = 0.f;
+#pragma unroll
+  for (int c = 0; c < kMaxChunks; ++c) {
+    wc[c] = c < jb.n_e ? fast_exp2(mc[c] - mmax) * lc[c] : 0.f;
+    lsum += wc[c];
+  }
+  const float inv = 1.0f / lsum;
+  uint4* dst = reinterpret_cast<uint4*>(args.out + ((size_t)head * args.seq + row) * D + g0 * 8);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int c = 0; c < kMaxChunks; ++c) {
+      const __half2* h = reinterpret_cast<const __half2*>(&t[c][g]);
+#pragma unroll
+      for (int k2 = 0; k2 < 4; ++k2) {
+        const float2 x = __half22float2(h[k2]);
+        f[2 * k2] = fmaf(x.x, wc[c], f[2 * k2]);
+        f[2 * k2 + 1] = fmaf(x.y, wc[c], f[2 * k2 + 1]);
+      }
+    }
+#pragma unroll
+    for (int k2 = 0; k2 < 8; ++k2) f[k2] *= inv;
+    dst[g] = pack16<bf16>(f);
   }
 }
 
@@ -800,28 +836,25 @@ inline size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 
 // Work decomposition and CTA schedule, shared by the workspace-size query and the launch.
 struct AttnPlan {
-  int q_tiles = 0, pairs = 0, chunk = 0, units = 0, ctas = 0;
+  int q_tiles = 0, chunk = 0, units = 0, ctas = 0;
   size_t stats_off = 0, o_off = 0, ws_bytes = 0;  // ws_bytes == 0: no split, no workspace
   std::vector<uint16_t> cta_off, unit_list;       // empty: round-robin over CTAs
+  std::vector<CombineJob> jobs;                   // split query tiles (one job per tile, all heads)
 };
 
-// Cost of a unit in "engine tiles" (tensor-core and exp work scale with the key tiles
-// both engines process), plus a fixed charge for the unit's prologue and epilogue
-// and, when split, for publishing and combining partials.
-inline int unit_cost(const Unit& un, int q_tiles) {
-  int c = 3;
-  for (int e = 0; e < 2; ++e) {
-    const int qe = 2 * un.pm + e;
-    if (qe < q_tiles) c += std::max(0, std::min(un.n, qe + 1 - un.j0));
-  }
-  return c + (un.n_chunks > 1 ? 2 : 0);
-}
+// Cost of a unit in key tiles (tensor-core and exp work scale with them), plus a fixed
+// charge for the unit's Q load, first scores and epilogue.
+inline int unit_cost(const Unit& un) { return 2 + un.n; }
+
+// Charge, in the same units, for the combine kernel that follows a split plan (kernel
+// boundary plus one pass over the partials).
+constexpr long kCombineCost = 6;
 
 // Longest-processing-time assignment of units to `ctas` CTAs; returns the makespan and
 // (optionally) fills the per-CTA lists.
-inline long lpt_schedule(int heads, int pairs, int q_tiles, int C, int units, int ctas, AttnPlan* out) {
+inline long lpt_schedule(int heads, int q_tiles, int C, int units, int ctas, AttnPlan* out) {
   std::vector<std::pair<int, int>> cost(units);  // (cost, unit)
-  for (int u = 0; u < units; ++u) cost[u] = {unit_cost(decode_unit(u, heads, pairs, q_tiles, C), q_tiles), u};
+  for (int u = 0; u < units; ++u) cost[u] = {unit_cost(decode_unit(u, heads, q_tiles, C)), u};
   std::stable_sort(cost.begin(), cost.end(), [](const std::pair<int, int>& a, const std::pair<int, int>& b) {
     return a.first > b.first;
   });
@@ -845,44 +878,54 @@ inline long lpt_schedule(int heads, int pairs, int q_tiles, int C, int units, in
   return *std::max_element(load.begin(), load.end());
 }
 
-inline int count_units(int heads, int pairs, int q_tiles, int C) {
-  int per_head = 0;
-  for (int pm = 0; pm < pairs; ++pm) per_head += (pair_tiles(pm, q_tiles) + C - 1) / C;
-  return heads * per_head;
+inline long count_units(int heads, int q_tiles, int C) {
+  long per_head = 0;
+  for (int qt = 0; qt < q_tiles; ++qt) per_head += (qt + C) / C;
+  return (long)heads * per_head;
 }
 
 AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
   AttnPlan p;
   p.q_tiles = (seq + kTile - 1) / kTile;
-  p.pairs = (p.q_tiles + 1) / 2;
-  const int max_nt = pair_tiles(p.pairs - 1, p.q_tiles);
+  const int max_nt = p.q_tiles;
   // Candidate chunk sizes: the whole key range (no split), or any smaller chunk when a
   // workspace is available and the units fit the schedule table.
   long best_span = -1;
   int best_c = max_nt;
   const int min_c = (max_nt + kMaxChunks - 1) / kMaxChunks;
   for (int C = max_nt; C >= min_c; --C) {
-    if (C < max_nt && !allow_split) break;
-    const int units = count_units(heads, p.pairs, p.q_tiles, C);
-    if (units > kMaxSched) {
-      if (C == max_nt) { best_c = C; best_span = -1; }
-      break;
-    }
-    const int ctas = std::min(units, sms);
-    const long span = lpt_schedule(heads, p.pairs, p.q_tiles, C, units, ctas, nullptr);
+    if (C < max_nt && (!allow_split || p.q_tiles > kMaxCombineJobs)) break;
+    const long units = count_units(heads, p.q_tiles, C);
+    if (units > kMaxSched) break;
+    const int ctas = (int)std::min<long>(units, sms);
+    const long span = lpt_schedule(heads, p.q_tiles, C, (int)units, ctas, nullptr) + (C < max_nt ? kCombineCost : 0);
     if (best_span < 0 || span < best_span) {
       best_span = span;
       best_c = C;
     }
   }
   p.chunk = best_c;
-  p.units = count_units(heads, p.pairs, p.q_tiles, p.chunk);
-  p.ctas = std::min(p.units, sms);
-  if (p.units <= kMaxSched && p.ctas <= kMaxCtas) lpt_schedule(heads, p.pairs, p.q_tiles, p.chunk, p.units, p.ctas, &p);
+  const long units = count_units(heads, p.q_tiles, p.chunk);
+  p.units = (int)std::min<long>(units, 1L << 30);
+  p.ctas = (int)std::min<long>(units, sms);
+  if (units <= kMaxSched && p.ctas <= kMaxCtas) lpt_schedule(heads, p.q_tiles, p.chunk, p.units, p.ctas, &p);
   if (p.chunk < max_nt) {
-    p.stats_off = round256((size_t)heads * p.q_tiles * sizeof(int));
-    p.o_off = p.stats_off + round256((size_t)p.units * 2 * 2 * kTile * sizeof(float));
-    p.ws_bytes = p.o_off + (size_t)p.units * 2 * kTile * (size_t)d * sizeof(__half);
+    p.stats_off = 0;
+    p.o_off = round256((size_t)p.units * 2 * kTile * sizeof(float));
+    p.ws_bytes = p.o_off + (size_t)p.units * kTile * (size_t)d * sizeof(__half);
+    int base = 0;  // per-head unit index of each query tile's chunk 0, in decode_unit order
+    for (int qt = p.q_tiles - 1; qt >= 0; --qt) {
+      const int nc = (qt + p.chunk) / p.chunk;
+      if (nc > 1) {
+        CombineJob j;
+        j.qt = (uint16_t)qt;
+        j.v0 = (uint16_t)base;
+        j.n_e = (uint16_t)nc;
+        j.pad = 0;
+        p.jobs.push_back(j);
+      }
+      base += nc;
+    }
   }
   return p;
 }
@@ -924,7 +967,6 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;
   a.heads = heads;
   a.q_tiles = plan.q_tiles;
-  a.pairs = plan.pairs;
   a.chunk = plan.chunk;
   a.units = plan.units;
   a.scale_log2 = scale * kLog2e;
@@ -934,7 +976,23 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
   for (size_t i = 0; i < plan.unit_list.size(); ++i) a.unit_list[i] = plan.unit_list[i];
   attn_fwd_bf16_kernel<D><<<plan.ctas, kAttnThreads, smem, st>>>(mq, mk, mv, mo, a);
-  return check_launch("nkl_attention");
+  rc = check_launch("nkl_attention");
+  if (rc || plan.jobs.empty()) return rc;
+  // split query tiles: merge the partials (programmatic dependent launch: the combine
+  // grid is scheduled early and waits on the device for the attention grid)
+  static CombineArgs ca;  // large kernel-parameter block, filled under the lock below
+  static std::mutex ca_mu;
+  std::lock_guard<std::mutex> lock(ca_mu);
+  ca.ws = static_cast<const unsigned char*>(ws);
+  ca.out = static_cast<bf16*>(out);
+  ca.heads = heads;
+  ca.seq = seq;
+  ca.n_jobs = (int)plan.jobs.size();
+  ca.ws_stats_off = plan.stats_off;
+  ca.ws_o_off = plan.o_off;
+  std::copy(plan.jobs.begin(), plan.jobs.end(), ca.job);
+  const dim3 grid((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 32)));
+  return launch_pdl(attn_combine_bf16_kernel<D>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
 }
 
 int check_attn(const char* op, int64_t heads, int64_t seq, int64_t d, int dtype) {

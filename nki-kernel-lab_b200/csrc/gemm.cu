@@ -132,6 +132,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         }
       }
     }
+    __syncwarp();  // the warp reconverges here: the CTA barrier below must see all 32 lanes
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (elect_one()) {
@@ -166,6 +167,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       const uint64_t t0 = globaltimer();
       while (!mbar_try_wait(&s.mma_done, 0) && globaltimer() - t0 < kWaitTimeoutNs) {}
     }
+    __syncwarp();  // the other lanes wait for the issuing lane before the CTA barrier and dealloc
   } else {
     // ---------------- epilogue (warps 2..5 = TMEM lane quadrants 2,3,0,1)
     const int q = warp & 3;

@@ -121,9 +121,9 @@ def _(a, b, naive):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
-# Split-KV workspaces of the bf16 attention kernel, one per (device, stream): zero-filled
-# once when created or grown; the kernel leaves them ready for the next call. Calls on
-# one stream are ordered, so they can share it; other streams get their own.
+# Split-KV workspaces of the bf16 attention kernel, one per (device, stream), grown on
+# demand (the kernels need no initialised contents). Calls on one stream are ordered, so
+# they can share it; other streams get their own.
 _attention_ws: dict = {}
 
 
@@ -131,7 +131,7 @@ def _attention_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.T
     key = (dev.index, stream)
     ws = _attention_ws.get(key)
     if ws is None or ws.numel() < nbytes:
-        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         _attention_ws[key] = ws
     return ws
 

@@ -134,8 +134,9 @@ def test_device_flag_clean_after_runs():
 
 
 def test_split_kv_workspace_path_matches_single_unit_path():
-    """nkl_attention_ws (key range split over SMs, partials combined) vs nkl_attention
-    (one unit per query tile) through the C ABI, and repeatable call to call."""
+    """nkl_attention_ws (key range split over SMs, partials combined by a second kernel)
+    vs nkl_attention (one unit per query tile) through the C ABI, repeatable call to call,
+    and independent of what the workspace held before (it needs no zeroing)."""
     import ctypes
     import math
 
@@ -148,7 +149,7 @@ def test_split_kv_workspace_path_matches_single_unit_path():
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     nbytes = N.lib.nkl_attention_workspace_size(H, S, D, N.BFLOAT16)
     assert nbytes > 0  # 128 query tiles do not fill 148 SMs: the split path is taken
-    ws = torch.zeros(nbytes, dtype=torch.uint8, device="cuda")
+    ws = torch.full((nbytes,), 0xA5, dtype=torch.uint8, device="cuda")
     o1, o2, o3 = (torch.empty_like(q) for _ in range(3))
     scale = 1 / math.sqrt(D)
     assert N.lib.nkl_attention(p(q), p(k), p(v), p(o1), H, S, D, scale, N.BFLOAT16, st) == N.OK
@@ -158,4 +159,3 @@ def test_split_kv_workspace_path_matches_single_unit_path():
     assert torch.equal(o2, o3)  # combine order is fixed: bit-identical across calls
     assert rel_err(o2.float().cpu().numpy(), o1.float().cpu().numpy()) < 3e-3
     _check_vs_oracle(o2, q.cpu(), k.cpu(), v.cpu())
-    assert int(torch.count_nonzero(ws[: H * (S // 128) * 4])) == 0  # counters left at zero
