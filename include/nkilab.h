@@ -6,8 +6,11 @@
  * allocates device memory, synchronises the stream or aborts: each call validates
  * its arguments on the host, enqueues its kernels asynchronously and returns an
  * nkl_status. nkl_last_error() gives a human-readable message for the most recent
- * failing call on the calling thread. No call keeps mutable global state on the
- * host, so calls are thread-safe as long as callers do not share output buffers.
+ * failing call on the calling thread. Host-side state is limited to caches filled
+ * once and then only read (per-device SM counts and kernel attributes, attention
+ * work plans per shape, the device address of the static softmax scratch), each
+ * behind a mutex or an atomic, so calls are thread-safe as long as callers do not
+ * share output buffers or workspaces.
  *
  * Layouts are row-major and dense (the innermost dimension is contiguous):
  *   row kernels  x, y      [rows, cols]

@@ -40,6 +40,8 @@
 
 #include <cuda_fp16.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -955,13 +957,13 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
     return fail(NKL_ERR_ARG, "nkl_attention_ws: workspace %zu B < required %zu B", ws_bytes, plan.ws_bytes);
   constexpr size_t smem = attn_smem_bytes<D>();
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64] = {};  // per device: the smem attribute is set (idempotent)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_attention: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   AttnArgs a;
   a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;

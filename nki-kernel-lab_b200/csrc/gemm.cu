@@ -17,6 +17,8 @@
 //               i overlaps the main loop of tile i+1
 // fp32 path: exact fp32 FMA tiled kernel on CUDA cores (tcgen05 has no full-precision
 // fp32 MMA; kind::tf32 would miss the reference's 1e-5 fp32 tolerance).
+#include <atomic>
+
 #include "common.cuh"
 #include "sm100.cuh"
 #include "tma_host.cuh"
@@ -301,14 +303,14 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
   const int grid = tiles < sm_count() ? tiles : sm_count();
   constexpr size_t smem = gemm_smem_bytes<BN, STAGES>();
   // The attribute is per device; setting the same value twice from racing threads is harmless.
-  static bool attr_set[64] = {false};
+  static std::atomic<bool> attr_set[64] = {};  // per device: the smem attribute is set (idempotent)
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
     cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_matmul: %s", cudaGetErrorString(e));
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   gemm_bf16_tc_kernel<BN, STAGES><<<grid, kGemmThreads, smem, st>>>(ma, mb, static_cast<bf16*>(c), M, N, K, m_tiles,
                                                                      n_tiles);
