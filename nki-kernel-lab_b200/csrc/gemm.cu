@@ -359,8 +359,16 @@ extern "C" int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int6
                 (long long)N);
   if (!is_aligned(a, 16) || !is_aligned(b, 16) || !is_aligned(c, 16))
     return fail(NKL_ERR_ALIGN, "nkl_matmul: bf16 operands must be 16-byte aligned");
-  const int64_t tiles256 = ((M + kBM - 1) / kBM) * ((N + 255) / 256);
-  if (tiles256 >= sm_count()) return launch_tc<256, 4>(a, b, c, (int)M, (int)N, (int)K, st);
+  // Tile width by how many tiles the SMs get. 256-column tiles read 96 B/clk of MMA
+  // operands from shared memory per SM and keep the tensor pipe fed; 128-column tiles
+  // need 128 B/clk, at the limit, so they are used only when 256-column tiles would
+  // leave more than half of the SMs idle, and 64-column tiles (more CTAs, smaller
+  // operands) when 128-column tiles would.
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  const int64_t tiles256 = m_tiles * ((N + 255) / 256);
+  const int64_t tiles128 = m_tiles * ((N + 127) / 128);
+  if (2 * tiles256 >= sm_count()) return launch_tc<256, 4>(a, b, c, (int)M, (int)N, (int)K, st);
+  if (2 * tiles128 <= sm_count()) return launch_tc<64, 8>(a, b, c, (int)M, (int)N, (int)K, st);
   return launch_tc<128, 6>(a, b, c, (int)M, (int)N, (int)K, st);
 }
 
