@@ -133,6 +133,17 @@ int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int6
 int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
                      int dtype, void* stream);
 
+/* Fused gate/up projection with SwiGLU: out[M, F] = silu(a . Wg) * (a . Wu), bf16 only.
+ * b_gate_up is [K, 2F] row-major with the columns of Wg and Wu interleaved in blocks of
+ * 128 (columns 256*i .. 256*i+127 = Wg[:, 128*i ..], the next 128 = Wu[:, 128*i ..]).
+ * Gate and up are rounded to bf16 before silu(gate) * up, as the unfused
+ * nkl_matmul -> nkl_matmul -> nkl_swiglu path rounds them, so both paths agree.
+ * F % 128 == 0, K % 8 == 0, 16-byte-aligned pointers.
+ * Replaces nkilab/model.py:87-88 (swiglu(matmul(h, Wg), matmul(h, Wu))), the fusion the
+ * reference lists as its next step (docs/STUDY_GUIDE.md:57). */
+int nkl_matmul_swiglu(const void* a, const void* b_gate_up, void* out, int64_t M, int64_t F,
+                      int64_t K, int dtype, void* stream);
+
 /* ---- causal attention (nkilab/kernels/attention.py) --------------------------- */
 
 /* out = softmax(q k^T * scale + causal mask) v per head, fp32 softmax statistics,

@@ -152,4 +152,13 @@ template <typename T> __device__ __forceinline__ float row_exp(float x) {
   else return __expf(x);
 }
 
+// silu(g) = g / (1 + exp(-g)) in fp32 (nkilab/kernels/norm.py:131-132): the accurate
+// expf and a true division for fp32 outputs, the fast forms when the product is rounded
+// to bf16. Shared by the SwiGLU row kernel and the GEMM's fused SwiGLU epilogue so the
+// two paths round identically.
+template <typename T> __device__ __forceinline__ float silu_f32(float g) {
+  if constexpr (sizeof(T) == 4) return g / (1.0f + expf(-g));
+  else return __fdividef(g, 1.0f + __expf(-g));
+}
+
 }  // namespace nkl

@@ -63,7 +63,12 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
   nt = r / gm;
 }
 
-template <int BN, int STAGES>
+// EPI: kEpiStore writes C = A.B in bf16. kEpiSwiglu takes B as [gate | up] column blocks
+// of 128 (see nkl_matmul_swiglu) and writes silu(gate) * up, each rounded to bf16 first
+// exactly as the unfused matmul -> swiglu path rounds them, into C[M, N/2].
+constexpr int kEpiStore = 0, kEpiSwiglu = 1;
+
+template <int BN, int STAGES, int EPI = kEpiStore>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     bf16* __restrict__ c, int M, int N, int K, int m_tiles, int n_tiles) {
@@ -186,6 +191,38 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       if (!ok) break;
       tc_fence_after();
       const int gm = mt * kBM + row;
+      if constexpr (EPI == kEpiSwiglu) {
+        static_assert(BN == 256, "the fused SwiGLU epilogue pairs 128 gate with 128 up columns");
+        const int F = N / 2;
+        bf16* orow = c + (int64_t)gm * F;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t rg[32], ru[32];
+          const uint32_t base = tmem + (uint32_t)(acc * BN + cc * 32) + ((uint32_t)(q * 32) << 16);
+          tmem_ld32(base, rg);
+          tmem_ld32(base + 128, ru);
+          tmem_wait_ld();
+          const int gn = nt * 128 + cc * 32;
+          if (gm < M) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              if (gn + v * 8 < F) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[v * 8 + e])));
+                  const float u = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[v * 8 + e])));
+                  f[e] = silu_f32<bf16>(g) * u;
+                }
+                *reinterpret_cast<uint4*>(orow + gn + v * 8) = pack16<bf16>(f);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s.acc_empty[acc]);
+        continue;
+      }
       bf16* crow = c + (int64_t)gm * N;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
@@ -280,7 +317,7 @@ gemm_naive_kernel(const T* __restrict__ A, const T* __restrict__ B, T* __restric
 
 // ------------------------------------------------------------------ host
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int EPI = kEpiStore>
 int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaStream_t st) {
   CUtensorMap ma, mb;
   {
@@ -307,13 +344,13 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(gemm_bf16_tc_kernel<BN, STAGES, EPI>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_matmul: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
-  gemm_bf16_tc_kernel<BN, STAGES><<<grid, kGemmThreads, smem, st>>>(ma, mb, static_cast<bf16*>(c), M, N, K, m_tiles,
-                                                                     n_tiles);
+  gemm_bf16_tc_kernel<BN, STAGES, EPI><<<grid, kGemmThreads, smem, st>>>(ma, mb, static_cast<bf16*>(c), M, N, K,
+                                                                          m_tiles, n_tiles);
   return check_launch("nkl_matmul");
 }
 
@@ -370,6 +407,22 @@ extern "C" int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int6
   if (2 * tiles256 >= sm_count()) return launch_tc<256, 4>(a, b, c, (int)M, (int)N, (int)K, st);
   if (2 * tiles128 <= sm_count()) return launch_tc<64, 8>(a, b, c, (int)M, (int)N, (int)K, st);
   return launch_tc<128, 6>(a, b, c, (int)M, (int)N, (int)K, st);
+}
+
+extern "C" int nkl_matmul_swiglu(const void* a, const void* b_gate_up, void* out, int64_t M, int64_t F, int64_t K,
+                                 int dtype, void* stream) {
+  int rc = check_gemm("nkl_matmul_swiglu", M, 2 * F, K, dtype);
+  if (rc) return rc;
+  if (dtype != NKL_BFLOAT16) return fail(NKL_ERR_DTYPE, "nkl_matmul_swiglu: bf16 only");
+  if (M == 0 || F == 0) return NKL_OK;
+  if (!a || !b_gate_up || !out) return fail(NKL_ERR_ARG, "nkl_matmul_swiglu: NULL pointer");
+  if (K == 0 || K % 8 != 0 || F % 128 != 0)
+    return fail(NKL_ERR_SHAPE, "nkl_matmul_swiglu: needs K > 0, K %% 8 == 0 and F %% 128 == 0 (got K=%lld F=%lld)",
+                (long long)K, (long long)F);
+  if (!is_aligned(a, 16) || !is_aligned(b_gate_up, 16) || !is_aligned(out, 16))
+    return fail(NKL_ERR_ALIGN, "nkl_matmul_swiglu: operands must be 16-byte aligned");
+  return launch_tc<256, 4, kEpiSwiglu>(a, b_gate_up, out, (int)M, (int)(2 * F), (int)K,
+                                        static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K, int dtype,

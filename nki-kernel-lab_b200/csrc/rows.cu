@@ -256,12 +256,6 @@ softmax_pass_div(const float* __restrict__ e_in, const float* __restrict__ s_in,
 
 // ------------------------------------------------------------------ SwiGLU
 
-template <typename T>
-__device__ __forceinline__ float silu_f32(float g) {
-  if constexpr (sizeof(T) == 4) return g / (1.0f + expf(-g));
-  else return __fdividef(g, 1.0f + __expf(-g));
-}
-
 constexpr int kSwigluThreads = 256;
 constexpr int kSwigluUnroll = 4;
 

@@ -121,6 +121,39 @@ def _(a, b, naive):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
+SWIGLU_BLOCK = 128  # column block of the interleaved [gate | up] weight of matmul_swiglu
+
+
+def interleave_gate_up(wg: torch.Tensor, wu: torch.Tensor) -> torch.Tensor:
+    """[K, F] gate and up weights -> the [K, 2F] layout nkl_matmul_swiglu reads: column
+    blocks of 128, gate block i followed by up block i."""
+    K, F = wg.shape
+    if wu.shape != wg.shape or F % SWIGLU_BLOCK:
+        raise ValueError(f"gate {tuple(wg.shape)} / up {tuple(wu.shape)}: need equal shapes and F % 128 == 0")
+    g = wg.reshape(K, F // SWIGLU_BLOCK, 1, SWIGLU_BLOCK)
+    u = wu.reshape(K, F // SWIGLU_BLOCK, 1, SWIGLU_BLOCK)
+    return torch.cat([g, u], dim=2).reshape(K, 2 * F).contiguous()
+
+
+@torch.library.custom_op("nkilab::matmul_swiglu", mutates_args=())
+def matmul_swiglu(a: torch.Tensor, b_gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(a @ Wg) * (a @ Wu) in one GEMM over the interleaved weight (bf16)."""
+    dev, dt, st = _prep(a, b_gate_up)
+    M, K = a.shape
+    K2, two_f = b_gate_up.shape
+    if K != K2 or two_f % (2 * SWIGLU_BLOCK):
+        raise ValueError(f"a {tuple(a.shape)}, b_gate_up {tuple(b_gate_up.shape)}: need matching K and 2F % 256 == 0")
+    out = torch.empty((M, two_f // 2), dtype=a.dtype, device=dev)
+    with torch.cuda.device(dev):
+        N.call("nkl_matmul_swiglu", a.data_ptr(), b_gate_up.data_ptr(), out.data_ptr(), M, two_f // 2, K, dt, st)
+    return out
+
+
+@matmul_swiglu.register_fake
+def _(a, b_gate_up):
+    return a.new_empty((a.shape[0], b_gate_up.shape[1] // 2))
+
+
 # Split-KV workspaces of the bf16 attention kernel, one per (device, stream), grown on
 # demand (the kernels need no initialised contents). Calls on one stream are ordered, so
 # they can share it; other streams get their own.

@@ -25,7 +25,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import ops
+from . import _torch_ops, ops
 
 
 @dataclass
@@ -97,6 +97,10 @@ def device_weights(block: DecoderBlock, dtype: torch.dtype, device) -> dict:
         w = {n: getattr(block, n).weight.detach().t().to(device=device, dtype=dtype).contiguous() for n in _WEIGHT_NAMES}
         w["norm1"] = block.norm1.weight.detach().to(device=device, dtype=dtype).contiguous()
         w["norm2"] = block.norm2.weight.detach().to(device=device, dtype=dtype).contiguous()
+        if dtype == torch.bfloat16 and w["wg"].shape[1] % _torch_ops.SWIGLU_BLOCK == 0:
+            # one GEMM for gate and up with SwiGLU in its epilogue (bit-identical to the
+            # unfused matmul -> matmul -> swiglu path)
+            w["wgu"] = _torch_ops.interleave_gate_up(w["wg"], w["wu"])
     cache[key] = (stamp, w)
     return w
 
@@ -116,7 +120,10 @@ def _forward_device(block: DecoderBlock, x: torch.Tensor, attention_variant: str
     a = a.view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B * S, d)
     x2 = x2 + ops.matmul(a, w["wo"])
     h = ops.rmsnorm(x2, w["norm2"], cfg.eps)
-    act = ops.swiglu(ops.matmul(h, w["wg"]), ops.matmul(h, w["wu"]))
+    if "wgu" in w:
+        act = torch.ops.nkilab.matmul_swiglu(h.contiguous(), w["wgu"])
+    else:
+        act = ops.swiglu(ops.matmul(h, w["wg"]), ops.matmul(h, w["wu"]))
     out = x2 + ops.matmul(act, w["wd"])
     return out.view(*lead, d)
 

@@ -123,3 +123,36 @@ def test_kernel_level_blocked_and_naive(rng):
     ref = lhsT.T @ rhs
     assert rel_err(mm.matmul_blocked(lhsT, rhs, BM=2, BN=2), ref) < 1e-5
     assert rel_err(mm.matmul_naive(lhsT, rhs), ref) < 1e-5
+
+
+@pytest.mark.parametrize("M,K,F", [(128, 64, 128), (300, 1000, 256), (1024, 4096, 1024), (4096, 512, 11008)])
+def test_matmul_swiglu_fused_equals_unfused(ops, M, K, F):
+    """One GEMM over the interleaved [gate | up] weight with SwiGLU in its epilogue gives
+    the same bf16 result as matmul -> matmul -> swiglu (both round gate and up to bf16
+    before silu(gate) * up), and matches the oracle's unfused path within 1e-2."""
+    from nkilab import _torch_ops
+
+    g = torch.Generator().manual_seed(M + K + F)
+    a = (torch.rand(M, K, generator=g) * 2 - 1).to(torch.bfloat16).cuda()
+    wg = (torch.randn(K, F, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    wu = (torch.randn(K, F, generator=g) * 0.05).to(torch.bfloat16).cuda()
+    fused = torch.ops.nkilab.matmul_swiglu(a, _torch_ops.interleave_gate_up(wg, wu))
+    unfused = ops.swiglu(ops.matmul(a, wg), ops.matmul(a, wu))
+    assert fused.shape == (M, F)
+    assert torch.equal(fused, unfused)
+    rows = torch.arange(0, M, max(1, M // 64))
+    ref = O.swiglu(O.matmul(a[rows].cpu(), wg.cpu()), O.matmul(a[rows].cpu(), wu.cpu()))
+    check_bf16(to_numpy(fused[rows].cpu()), to_numpy(ref))
+
+
+def test_matmul_swiglu_rejects_bad_shapes(ops):
+    from nkilab import _native as N
+
+    a = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(64, 2 * 100, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(128, 100, dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = N.lib.nkl_matmul_swiglu(a.data_ptr(), b.data_ptr(), out.data_ptr(), 128, 100, 64, N.BFLOAT16, st)
+    assert rc == N.ERR_SHAPE and "F % 128" in N.lib.nkl_last_error().decode()
+    rc = N.lib.nkl_matmul_swiglu(a.data_ptr(), b.data_ptr(), out.data_ptr(), 128, 128, 64, N.FLOAT32, st)
+    assert rc == N.ERR_DTYPE
