@@ -173,6 +173,26 @@ int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, voi
                      size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim,
                      float scale, int dtype, void* stream);
 
+/* Rotary position embedding (rotate-half convention) of x [heads, seq, head_dim] into
+ * out (may equal x): for i < head_dim/2, theta_i = base^(-2i/head_dim), angle =
+ * (s + pos_offset) * theta_i, out[i] = x[i] cos - x[i+d/2] sin, out[i+d/2] =
+ * x[i+d/2] cos + x[i] sin, in fp32 with one rounding. head_dim a multiple of 16 (bf16)
+ * or 8 (fp32), 16-byte-aligned pointers, positions below 2^24.
+ * No reference counterpart: rotary embeddings are the reference's listed next step
+ * (README.md:89). */
+int nkl_rope(const void* x, void* out, int64_t heads, int64_t seq, int64_t head_dim, float base,
+             int64_t pos_offset, int dtype, void* stream);
+
+/* Grouped-query / multi-query attention: q, out [heads, seq, head_dim]; k, v [kv_heads,
+ * seq, head_dim] with kv_heads dividing heads; query head h attends with key/value head
+ * h / (heads / kv_heads). Same numerics, layouts, workspace (size from
+ * nkl_attention_workspace_size(heads, ...); NULL = no split) and errors as
+ * nkl_attention_ws; kv_heads == heads is plain multi-head attention.
+ * No reference counterpart: GQA/MQA is the reference's listed next step (README.md:89). */
+int nkl_attention_gqa(const void* q, const void* k, const void* v, void* out, void* workspace,
+                      size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq,
+                      int64_t head_dim, float scale, int dtype, void* stream);
+
 /* Bytes of device workspace nkl_attention_naive needs: fp32 scores and dtype
  * probabilities, each [heads, seq, seq]. */
 size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype);

@@ -158,6 +158,7 @@ constexpr size_t attn_smem_bytes() {
 struct AttnArgs {
   unsigned char* ws;  // NULL when no query tile is split
   int heads, q_tiles, chunk, units;
+  int kv_group;  // query heads per key/value head (1 = multi-head, heads = multi-query)
   float scale_log2;
   size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (max, sum) and O regions
   int n_ctas_listed;              // > 0: cta_off / unit_list give each CTA's units
@@ -291,7 +292,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
         k_armed[ks] = (int)((kc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, (un.j0 + t) * kTile, un.head);
+          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, (un.j0 + t) * kTile,
+                      un.head / args.kv_group);
         ++kc;
         return true;
       };
@@ -301,7 +303,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
         v_armed[vs] = (int)((vc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, (un.j0 + t) * kTile, un.head);
+          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, (un.j0 + t) * kTile,
+                      un.head / args.kv_group);
         ++vc;
         return true;
       };
@@ -655,7 +658,7 @@ constexpr int kF32Keys = 32;
 
 __global__ void __launch_bounds__(128)
 attn_fwd_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
-                    float* __restrict__ out, int seq, int d, float scale) {
+                    float* __restrict__ out, int seq, int d, float scale, int kv_group) {
   __shared__ float ks[kF32Keys][129];
   __shared__ float vs[kF32Keys][128];
   __shared__ float qs[kF32Rows][128];
@@ -663,8 +666,8 @@ attn_fwd_f32_kernel(const float* __restrict__ q, const float* __restrict__ k, co
   const int r0 = blockIdx.x * kF32Rows;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float* qh = q + (int64_t)head * seq * d;
-  const float* kh = k + (int64_t)head * seq * d;
-  const float* vh = v + (int64_t)head * seq * d;
+  const float* kh = k + (int64_t)(head / kv_group) * seq * d;
+  const float* vh = v + (int64_t)(head / kv_group) * seq * d;
   for (int i = threadIdx.x; i < kF32Rows * d; i += 128) {
     const int rr = i / d, cc = i % d;
     qs[rr][cc] = (r0 + rr < seq) ? qh[(int64_t)(r0 + rr) * d + cc] : 0.f;
@@ -945,12 +948,12 @@ const AttnPlan& cached_plan(int heads, int seq, int d, bool allow_split) {
 }
 
 template <int D>
-int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int heads, int seq, float scale,
-                     void* ws, size_t ws_bytes, cudaStream_t st) {
+int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int heads, int kv_heads, int seq,
+                     float scale, void* ws, size_t ws_bytes, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo;
   int rc = make_qkv_map(&mq, q, heads, seq, D, "nkl_attention(q)");
-  if (!rc) rc = make_qkv_map(&mk, k, heads, seq, D, "nkl_attention(k)");
-  if (!rc) rc = make_qkv_map(&mv, v, heads, seq, D, "nkl_attention(v)");
+  if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, "nkl_attention(k)");
+  if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, "nkl_attention(v)");
   if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, "nkl_attention(out)");
   if (rc) return rc;
   const AttnPlan& plan = cached_plan(heads, seq, D, ws != nullptr);
@@ -968,6 +971,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   AttnArgs a;
   a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;
   a.heads = heads;
+  a.kv_group = heads / kv_heads;
   a.q_tiles = plan.q_tiles;
   a.chunk = plan.chunk;
   a.units = plan.units;
@@ -1019,27 +1023,47 @@ int attention_read_and_clear_device_error() {
 
 using namespace nkl;
 
-extern "C" int nkl_attention(const void* q, const void* k, const void* v, void* out, int64_t heads, int64_t seq,
-                             int64_t head_dim, float scale, int dtype, void* stream) {
-  int rc = check_attn("nkl_attention", heads, seq, head_dim, dtype);
+namespace {
+
+// Shared body of the fused attention entry points: heads query heads read K and V
+// head h / (heads / kv_heads); a NULL workspace (or fp32) keeps every query tile in
+// one unit.
+int attention_impl(const char* op, const void* q, const void* k, const void* v, void* out, void* workspace,
+                   size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq, int64_t head_dim,
+                   float scale, int dtype, void* stream) {
+  int rc = check_attn(op, heads, seq, head_dim, dtype);
   if (rc) return rc;
   if (heads == 0 || seq == 0) return NKL_OK;
-  if (!q || !k || !v || !out) return fail(NKL_ERR_ARG, "nkl_attention: NULL pointer");
+  if (kv_heads < 1 || kv_heads > heads || heads % kv_heads != 0)
+    return fail(NKL_ERR_SHAPE, "%s: kv_heads must divide heads (got heads=%lld kv_heads=%lld)", op, (long long)heads,
+                (long long)kv_heads);
+  if (!q || !k || !v || !out) return fail(NKL_ERR_ARG, "%s: NULL pointer", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (dtype == NKL_FLOAT32) {
     dim3 grid((unsigned)((seq + kF32Rows - 1) / kF32Rows), (unsigned)heads);
     attn_fwd_f32_kernel<<<grid, 128, 0, st>>>(static_cast<const float*>(q), static_cast<const float*>(k),
                                               static_cast<const float*>(v), static_cast<float*>(out), (int)seq,
-                                              (int)head_dim, scale);
-    return check_launch("nkl_attention");
+                                              (int)head_dim, scale, (int)(heads / kv_heads));
+    return check_launch(op);
   }
   if (head_dim != 64 && head_dim != 128)
-    return fail(NKL_ERR_SHAPE, "nkl_attention: bf16 head_dim must be 64 or 128 (got %lld); pad on the host",
+    return fail(NKL_ERR_SHAPE, "%s: bf16 head_dim must be 64 or 128 (got %lld); pad on the host", op,
                 (long long)head_dim);
   if (!is_aligned(q, 16) || !is_aligned(k, 16) || !is_aligned(v, 16) || !is_aligned(out, 16))
-    return fail(NKL_ERR_ALIGN, "nkl_attention: bf16 tensors must be 16-byte aligned");
-  if (head_dim == 64) return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)seq, scale, nullptr, 0, st);
-  return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)seq, scale, nullptr, 0, st);
+    return fail(NKL_ERR_ALIGN, "%s: bf16 tensors must be 16-byte aligned", op);
+  if (workspace && !is_aligned(workspace, 256)) return fail(NKL_ERR_ALIGN, "%s: workspace not 256-byte aligned", op);
+  if (head_dim == 64)
+    return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
+                                workspace ? workspace_bytes : 0, st);
+  return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
+                               workspace ? workspace_bytes : 0, st);
+}
+
+}  // namespace
+
+extern "C" int nkl_attention(const void* q, const void* k, const void* v, void* out, int64_t heads, int64_t seq,
+                             int64_t head_dim, float scale, int dtype, void* stream) {
+  return attention_impl("nkl_attention", q, k, v, out, nullptr, 0, heads, heads, seq, head_dim, scale, dtype, stream);
 }
 
 extern "C" size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
@@ -1051,22 +1075,15 @@ extern "C" size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64
 extern "C" int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, void* workspace,
                                 size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim, float scale,
                                 int dtype, void* stream) {
-  if (workspace == nullptr || dtype != NKL_BFLOAT16)
-    return nkl_attention(q, k, v, out, heads, seq, head_dim, scale, dtype, stream);
-  int rc = check_attn("nkl_attention_ws", heads, seq, head_dim, dtype);
-  if (rc) return rc;
-  if (heads == 0 || seq == 0) return NKL_OK;
-  if (!q || !k || !v || !out) return fail(NKL_ERR_ARG, "nkl_attention_ws: NULL pointer");
-  if (head_dim != 64 && head_dim != 128)
-    return fail(NKL_ERR_SHAPE, "nkl_attention_ws: bf16 head_dim must be 64 or 128 (got %lld); pad on the host",
-                (long long)head_dim);
-  if (!is_aligned(q, 16) || !is_aligned(k, 16) || !is_aligned(v, 16) || !is_aligned(out, 16))
-    return fail(NKL_ERR_ALIGN, "nkl_attention_ws: bf16 tensors must be 16-byte aligned");
-  if (!is_aligned(workspace, 256)) return fail(NKL_ERR_ALIGN, "nkl_attention_ws: workspace not 256-byte aligned");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (head_dim == 64)
-    return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)seq, scale, workspace, workspace_bytes, st);
-  return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)seq, scale, workspace, workspace_bytes, st);
+  return attention_impl("nkl_attention_ws", q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr,
+                        workspace_bytes, heads, heads, seq, head_dim, scale, dtype, stream);
+}
+
+extern "C" int nkl_attention_gqa(const void* q, const void* k, const void* v, void* out, void* workspace,
+                                 size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq,
+                                 int64_t head_dim, float scale, int dtype, void* stream) {
+  return attention_impl("nkl_attention_gqa", q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr,
+                        workspace_bytes, heads, kv_heads, seq, head_dim, scale, dtype, stream);
 }
 
 extern "C" size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype) {

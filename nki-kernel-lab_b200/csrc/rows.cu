@@ -295,6 +295,45 @@ swiglu_scalar_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __rest
     y[i] = from_f32<T>(silu_f32<T>(to_f32(g[i])) * to_f32(u[i]));
 }
 
+// ------------------------------------------------------------------ rotary embedding
+
+// Rotary position embedding, rotate-half convention: for i < d/2, with
+// theta_i = base^(-2i/d) (computed in fp32 as 1 / powf(base, 2i/d)) and angle = pos * theta_i,
+//   out[i]       = x[i] * cos(angle) - x[i + d/2] * sin(angle)
+//   out[i + d/2] = x[i + d/2] * cos(angle) + x[i] * sin(angle)
+// in fp32 with one rounding to the output dtype; pos = row index within the sequence +
+// pos_offset. A thread handles one 16-byte vector of each half. No reference counterpart
+// (rotary embeddings are the reference's listed next step, README.md:89).
+template <typename T>
+__global__ void __launch_bounds__(256)
+rope_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int seq, int d, float base, int pos_offset) {
+  constexpr int V = Vec16<T>::N;
+  pdl_enter();
+  const int half_vecs = d / 2 / V;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * half_vecs) return;
+  const int64_t row = i / half_vecs;
+  const int c0 = (int)(i - row * half_vecs) * V;  // first column of this thread's vector in the first half
+  const float pos = (float)((int)(row % seq) + pos_offset);
+  const T* xr = x + row * d;
+  T* yr = y + row * d;
+  Vec16<T> a, b;
+  a.raw = ld_stream(xr + c0);
+  b.raw = ld_stream(xr + c0 + d / 2);
+  float oa[V], ob[V];
+#pragma unroll
+  for (int e = 0; e < V; ++e) {
+    const float inv_freq = 1.0f / powf(base, (float)(2 * (c0 + e)) / (float)d);
+    float sn, cs;
+    sincosf(pos * inv_freq, &sn, &cs);
+    const float xa = a.get(e), xb = b.get(e);
+    oa[e] = xa * cs - xb * sn;
+    ob[e] = xb * cs + xa * sn;
+  }
+  st_stream(yr + c0, pack16<T>(oa));
+  st_stream(yr + c0 + d / 2, pack16<T>(ob));
+}
+
 // ------------------------------------------------------------------ dispatch
 
 template <typename T>
@@ -526,4 +565,28 @@ extern "C" int nkl_softmax_unfused_static(const void* x, void* out, int64_t rows
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == NKL_FLOAT32 ? softmax_unfused_launch<float>(x, out, scratch, rows, cols, st)
                               : softmax_unfused_launch<bf16>(x, out, scratch, rows, cols, st);
+}
+
+extern "C" int nkl_rope(const void* x, void* out, int64_t heads, int64_t seq, int64_t head_dim, float base,
+                        int64_t pos_offset, int dtype, void* stream) {
+  using namespace nkl;
+  if (!valid_dtype(dtype)) return fail(NKL_ERR_DTYPE, "nkl_rope: unsupported dtype %d", dtype);
+  const int64_t V = 16 / (int64_t)dtype_size(dtype);
+  if (heads < 0 || seq < 0 || head_dim <= 0 || head_dim % (2 * V) != 0 || head_dim > 65536)
+    return fail(NKL_ERR_SHAPE, "nkl_rope: head_dim must be a positive multiple of %lld (got %lld)", (long long)(2 * V),
+                (long long)head_dim);
+  if (!(base > 1.0f) || pos_offset < 0 || seq + pos_offset > (1LL << 24))
+    return fail(NKL_ERR_ARG, "nkl_rope: need base > 1 and 0 <= positions < 2^24");
+  if (heads == 0 || seq == 0) return NKL_OK;
+  if (!x || !out) return fail(NKL_ERR_ARG, "nkl_rope: NULL pointer");
+  if (!is_aligned(x, 16) || !is_aligned(out, 16)) return fail(NKL_ERR_ALIGN, "nkl_rope: tensors must be 16-byte aligned");
+  const int64_t rows = heads * seq;
+  const int64_t threads = rows * (head_dim / 2 / V);
+  const dim3 grid((unsigned)((threads + 255) / 256));
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (dtype == NKL_BFLOAT16)
+    return launch_pdl(rope_kernel<bf16>, grid, dim3(256), 0, st, "nkl_rope", static_cast<const bf16*>(x),
+                      static_cast<bf16*>(out), rows, (int)seq, (int)head_dim, base, (int)pos_offset);
+  return launch_pdl(rope_kernel<float>, grid, dim3(256), 0, st, "nkl_rope", static_cast<const float*>(x),
+                    static_cast<float*>(out), rows, (int)seq, (int)head_dim, base, (int)pos_offset);
 }

@@ -43,12 +43,14 @@ SIGNATURES = {
     "nkl_softmax_unfused": (_int, [_p, _p, _p, _sz, _i64, _i64, _int, _p]),
     "nkl_softmax_unfused_static": (_int, [_p, _p, _i64, _i64, _int, _p]),
     "nkl_swiglu": (_int, [_p, _p, _p, _i64, _i64, _int, _p]),
+    "nkl_rope": (_int, [_p, _p, _i64, _i64, _i64, _f, _i64, _int, _p]),
     "nkl_matmul": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_naive": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_swiglu": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_attention": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "nkl_attention_ws": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
+    "nkl_attention_gqa": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_naive_workspace_size": (_sz, [_i64, _i64, _int]),
     "nkl_attention_naive": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
 }

@@ -121,6 +121,22 @@ def _(a, b, naive):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
+@torch.library.custom_op("nkilab::rope", mutates_args=())
+def rope(x: torch.Tensor, base: float, pos_offset: int) -> torch.Tensor:
+    """Rotary position embedding (rotate-half) of x [heads, seq, head_dim]."""
+    dev, dt, st = _prep(x)
+    H, S, d = x.shape
+    out = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        N.call("nkl_rope", x.data_ptr(), out.data_ptr(), H, S, d, base, pos_offset, dt, st)
+    return out
+
+
+@rope.register_fake
+def _(x, base, pos_offset):
+    return torch.empty_like(x)
+
+
 SWIGLU_BLOCK = 128  # column block of the interleaved [gate | up] weight of matmul_swiglu
 
 
@@ -173,11 +189,20 @@ def _attention_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.T
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, naive: bool) -> torch.Tensor:
     dev, dt, st = _prep(q, k, v)
     H, S, d = q.shape
-    if k.shape != q.shape or v.shape != q.shape:
-        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)} must match")
+    Hkv = k.shape[0]
+    if k.shape != v.shape or k.shape[1:] != q.shape[1:] or Hkv < 1 or H % Hkv:
+        raise ValueError(f"q {tuple(q.shape)}, k {tuple(k.shape)}, v {tuple(v.shape)}: k and v must match, "
+                         "and their head count divide q's")
+    if naive and Hkv != H:
+        raise ValueError("the naive variant needs as many key/value heads as query heads")
     out = torch.empty_like(q)
     with torch.cuda.device(dev):
-        if naive:
+        if Hkv != H:  # grouped-query / multi-query attention
+            nbytes = N.lib.nkl_attention_workspace_size(H, S, d, dt)
+            ws = _attention_workspace(dev, st, nbytes) if nbytes else None
+            N.call("nkl_attention_gqa", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                   ws.data_ptr() if ws is not None else None, nbytes, H, Hkv, S, d, scale, dt, st)
+        elif naive:
             nbytes = N.lib.nkl_attention_naive_workspace_size(H, S, dt)
             ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
             N.call("nkl_attention_naive", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), ws.data_ptr(),

@@ -113,6 +113,9 @@ def attention(q, k, v, variant: str = "flash_pipelined"):
     are cropped). Every "flash*" variant runs the same tcgen05 flash kernel (the
     reference's variants share numerics, tests/test_attention.py:67-70);
     "naive" materialises the scores and probabilities.
+
+    Extension beyond the reference: k and v may carry fewer heads than q (grouped-query
+    or multi-query attention); query head h then uses key/value head h // (H // Hkv).
     """
     if variant not in ATTENTION_VARIANTS:
         raise KeyError(variant)
@@ -132,3 +135,13 @@ def attention(q, k, v, variant: str = "flash_pipelined"):
     if dp != d:
         o = o[..., :d].contiguous()
     return _like_input(o, q)
+
+
+def rope(x, base: float = 10000.0, pos_offset: int = 0):
+    """Rotary position embedding, rotate-half convention, of x: [H, S, d] (extension
+    beyond the reference, which lists rotary embeddings as not done, README.md:89).
+    Position of row s is s + pos_offset; theta_i = base^(-2i/d). NumPy or torch in,
+    same kind out."""
+    xd = _to_device(x).contiguous()
+    o = torch.ops.nkilab.rope(xd, float(base), int(pos_offset))
+    return _like_input(o, x)

@@ -159,3 +159,39 @@ def test_split_kv_workspace_path_matches_single_unit_path():
     assert torch.equal(o2, o3)  # combine order is fixed: bit-identical across calls
     assert rel_err(o2.float().cpu().numpy(), o1.float().cpu().numpy()) < 3e-3
     _check_vs_oracle(o2, q.cpu(), k.cpu(), v.cpu())
+
+
+@pytest.mark.parametrize("H,Hkv,S,D,dt", [(8, 2, 2048, 128, torch.bfloat16), (8, 1, 1000, 64, torch.bfloat16),
+                                          (4, 2, 300, 96, torch.bfloat16), (4, 1, 257, 64, torch.float32)])
+def test_grouped_query_attention_equals_repeated_heads(H, Hkv, S, D, dt):
+    """k, v with Hkv heads: query head h uses key/value head h // (H // Hkv). The result
+    equals plain attention on k, v with each head repeated H // Hkv times (same kernel,
+    same data), bit for bit, and the oracle within the attention tolerance."""
+    from nkilab import ops
+
+    g = torch.Generator().manual_seed(H * 1000 + Hkv * 100 + S)
+    q = torch.randn(H, S, D, generator=g).to(dt)
+    k = torch.randn(Hkv, S, D, generator=g).to(dt)
+    v = torch.randn(Hkv, S, D, generator=g).to(dt)
+    rep = H // Hkv
+    got = ops.attention(q.cuda(), k.cuda(), v.cuda())
+    full = ops.attention(q.cuda(), k.repeat_interleave(rep, 0).cuda(), v.repeat_interleave(rep, 0).cuda())
+    assert torch.equal(got, full)
+    if dt == torch.float32:
+        ref = torch.nn.functional.scaled_dot_product_attention(q, k.repeat_interleave(rep, 0), v.repeat_interleave(rep, 0),
+                                                               is_causal=True)
+        assert float((got.cpu() - ref).abs().max()) < 2e-5
+    else:
+        ref = O.attention_flash(q[:2], k.repeat_interleave(rep, 0)[:2], v.repeat_interleave(rep, 0)[:2])
+        assert rel_err(to_numpy(got[:2].cpu()), to_numpy(ref)) < 3e-3
+
+
+def test_grouped_query_attention_rejects_bad_head_counts():
+    from nkilab import _native as N
+
+    q = torch.zeros(6, 128, 64, dtype=torch.bfloat16, device="cuda")
+    kv = torch.zeros(4, 128, 64, dtype=torch.bfloat16, device="cuda")
+    st = torch.cuda.current_stream().cuda_stream
+    rc = N.lib.nkl_attention_gqa(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), None, 0, 6, 4, 128, 64,
+                                 0.125, N.BFLOAT16, st)
+    assert rc == N.ERR_SHAPE and "kv_heads must divide heads" in N.lib.nkl_last_error().decode()

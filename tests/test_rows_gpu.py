@@ -189,3 +189,44 @@ def test_c_abi_direct_call():
     assert rc == N.OK
     N.check_device(st)
     check_close(to_numpy(y), to_numpy(O.rmsnorm(x, w)))
+
+
+def _rope_reference(x: torch.Tensor, base: float, pos_offset: int) -> torch.Tensor:
+    """Rotate-half rotary embedding in fp64 (the Llama / Hugging Face formulation)."""
+    H, S, d = x.shape
+    inv_freq = 1.0 / (base ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+    ang = (torch.arange(S, dtype=torch.float64) + pos_offset)[:, None] * inv_freq[None, :]
+    cos, sin = torch.cos(ang), torch.sin(ang)
+    x1, x2 = x[..., : d // 2].double(), x[..., d // 2:].double()
+    return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1)
+
+
+@pytest.mark.parametrize("H,S,d,dt,base,off", [(8, 2048, 128, torch.bfloat16, 10000.0, 0),
+                                               (2, 300, 64, torch.float32, 10000.0, 0),
+                                               (4, 129, 128, torch.float32, 500000.0, 4000),
+                                               (1, 17, 16, torch.bfloat16, 10000.0, 7)])
+def test_rope_matches_fp64_reference(H, S, d, dt, base, off):
+    from nkilab import ops
+
+    g = torch.Generator().manual_seed(H + S + d)
+    x = torch.randn(H, S, d, generator=g).to(dt)
+    got = ops.rope(x.cuda(), base, off).cpu()
+    ref = _rope_reference(x, base, off)
+    err = (got.double() - ref).abs().max().item()
+    if dt == torch.float32:
+        # fp32 angle = pos * theta carries ~pos * 2^-24 rad of rounding, as in any fp32 RoPE
+        assert err < 1e-5 + (S + off) * 2.0 ** -22
+    else:
+        assert err / ref.abs().max().item() < 1e-2
+
+
+def test_rope_in_place_and_bad_shapes():
+    from nkilab import _native as N
+
+    x = torch.randn(2, 64, 128, device="cuda").to(torch.bfloat16)
+    want = torch.ops.nkilab.rope(x, 10000.0, 0)
+    st = torch.cuda.current_stream().cuda_stream
+    assert N.lib.nkl_rope(x.data_ptr(), x.data_ptr(), 2, 64, 128, 10000.0, 0, N.BFLOAT16, st) == N.OK
+    assert torch.equal(x, want)
+    assert N.lib.nkl_rope(x.data_ptr(), x.data_ptr(), 2, 64, 120, 10000.0, 0, N.BFLOAT16, st) == N.ERR_SHAPE
+    assert N.lib.nkl_rope(x.data_ptr(), x.data_ptr(), 2, 64, 128, 1.0, 0, N.BFLOAT16, st) == N.ERR_ARG
