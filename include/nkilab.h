@@ -173,6 +173,14 @@ int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, voi
                      size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim,
                      float scale, int dtype, void* stream);
 
+/* Residual add fused with RMSNorm: sum_out = x + residual (rounded to dtype, as the
+ * reference's host-side residual add in x.dtype), out = rmsnorm(sum_out, weight, eps)
+ * with nkl_rmsnorm's rounding points; one pass over x and residual.
+ * Replaces nkilab/model.py:86-87 (x = x + ...; rmsnorm(x, ...)), the fusion the
+ * reference lists as its next step (docs/STUDY_GUIDE.md:57). */
+int nkl_add_rmsnorm(const void* x, const void* residual, const void* weight, void* sum_out,
+                    void* out, int64_t rows, int64_t cols, float eps, int dtype, void* stream);
+
 /* Rotary position embedding (rotate-half convention) of x [heads, seq, head_dim] into
  * out (may equal x): for i < head_dim/2, theta_i = base^(-2i/head_dim), angle =
  * (s + pos_offset) * theta_i, out[i] = x[i] cos - x[i+d/2] sin, out[i+d/2] =

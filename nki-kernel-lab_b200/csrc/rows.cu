@@ -18,6 +18,7 @@
 // output dtype at the end (rmsnorm rounds x*rstd to fp32 before the weight multiply,
 // norm.py:114-116; fused softmax multiplies by a reciprocal, norm.py:84-87; unfused
 // softmax divides, norm.py:142).
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -295,6 +296,74 @@ swiglu_scalar_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __rest
     y[i] = from_f32<T>(silu_f32<T>(to_f32(g[i])) * to_f32(u[i]));
 }
 
+// ------------------------------------------------------------------ residual add + RMSNorm
+
+// s = x + r rounded to the dtype (the reference adds the residual on the host in x.dtype,
+// nkilab/model.py:86,89), written out, then y = rmsnorm(s) with the same rounding points
+// as rmsnorm_warp_kernel: one pass over x and r instead of an add kernel and a norm kernel.
+template <typename T, int NV>
+__global__ void __launch_bounds__(kRmsWarpsPerBlock * 32)
+add_rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
+                        T* __restrict__ s_out, T* __restrict__ y, int64_t rows, int cols, float inv_cols, float eps) {
+  constexpr int V = Vec16<T>::N;
+  pdl_enter();
+  const int64_t row = (int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int nvec = cols / V;
+  Vec16<T> sv[NV];
+  {
+    Vec16<T> rv[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      if (j < nvec) {
+        sv[i].raw = ld_stream(x + row * cols + (int64_t)j * V);
+        rv[i].raw = ld_stream(res + row * cols + (int64_t)j * V);
+      } else {
+        sv[i].raw = rv[i].raw = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      float f[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) f[e] = sv[i].get(e) + rv[i].get(e);
+      sv[i].raw = pack16<T>(f);  // the sum, rounded to the dtype
+      const int j = i * 32 + lane;
+      if (j < nvec) st_stream(s_out + row * cols + (int64_t)j * V, sv[i].raw);
+    }
+  }
+  float ssq = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+#pragma unroll
+    for (int e = 0; e < V; ++e) { const float f = sv[i].get(e); ssq += f * f; }
+  }
+  ssq = warp_sum(ssq);
+  const float rstd = rsqrtf(ssq * inv_cols + eps);
+  T* yr = y + row * cols;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (j < nvec) {
+      Vec16<T> wv;
+      wv.raw = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)j * V));
+      float o[V];
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = (sv[i].get(e) * rstd) * wv.get(e);  // fp32 s * rstd, then * weight
+      st_stream(yr + (int64_t)j * V, pack16<T>(o));
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+add_scalar_kernel(const T* __restrict__ x, const T* __restrict__ r, T* __restrict__ s, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    s[i] = from_f32<T>(to_f32(x[i]) + to_f32(r[i]));
+}
+
 // ------------------------------------------------------------------ rotary embedding
 
 // Rotary position embedding, rotate-half convention: for i < d/2, with
@@ -460,6 +529,52 @@ extern "C" int nkl_rmsnorm(const void* x, const void* weight, void* out, int64_t
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return dtype == NKL_FLOAT32 ? rmsnorm_launch<float>(x, weight, out, rows, cols, eps, st)
                               : rmsnorm_launch<bf16>(x, weight, out, rows, cols, eps, st);
+}
+
+extern "C" int nkl_add_rmsnorm(const void* x, const void* residual, const void* weight, void* sum_out, void* out,
+                               int64_t rows, int64_t cols, float eps, int dtype, void* stream) {
+  int rc = check_rows("nkl_add_rmsnorm", rows, cols, dtype);
+  if (rc) return rc;
+  if (rows == 0) return NKL_OK;
+  if (!x || !residual || !weight || !sum_out || !out) return fail(NKL_ERR_ARG, "nkl_add_rmsnorm: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const float inv_cols = (float)(1.0 / (double)cols);
+  auto fused = [&](auto tag) -> int {
+    using T = decltype(tag);
+    const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
+    const dim3 grid((unsigned)((rows + kRmsWarpsPerBlock - 1) / kRmsWarpsPerBlock)), blk(kRmsWarpsPerBlock * 32);
+    const T* xp = static_cast<const T*>(x);
+    const T* rp = static_cast<const T*>(residual);
+    const T* wp = static_cast<const T*>(weight);
+    T* sp = static_cast<T*>(sum_out);
+    T* yp = static_cast<T*>(out);
+    const int c = (int)cols;
+    switch (nv) {
+      case 1: return launch_pdl(add_rmsnorm_warp_kernel<T, 1>, grid, blk, 0, st, "nkl_add_rmsnorm", xp, rp, wp, sp, yp, rows, c, inv_cols, eps);
+      case 2: return launch_pdl(add_rmsnorm_warp_kernel<T, 2>, grid, blk, 0, st, "nkl_add_rmsnorm", xp, rp, wp, sp, yp, rows, c, inv_cols, eps);
+      case 4: return launch_pdl(add_rmsnorm_warp_kernel<T, 4>, grid, blk, 0, st, "nkl_add_rmsnorm", xp, rp, wp, sp, yp, rows, c, inv_cols, eps);
+      case 8: return launch_pdl(add_rmsnorm_warp_kernel<T, 8>, grid, blk, 0, st, "nkl_add_rmsnorm", xp, rp, wp, sp, yp, rows, c, inv_cols, eps);
+      default: return launch_pdl(add_rmsnorm_warp_kernel<T, 16>, grid, blk, 0, st, "nkl_add_rmsnorm", xp, rp, wp, sp, yp, rows, c, inv_cols, eps);
+    }
+  };
+  const bool vec = dtype == NKL_FLOAT32 ? row_vectorizable<float>(cols, x, out, weight) &&
+                                              is_aligned(residual, 16) && is_aligned(sum_out, 16)
+                                        : row_vectorizable<bf16>(cols, x, out, weight) &&
+                                              is_aligned(residual, 16) && is_aligned(sum_out, 16);
+  if (vec) return dtype == NKL_FLOAT32 ? fused(float{}) : fused(bf16{});
+  // other shapes: the add, then the norm of the rounded sum (same results, two passes)
+  const int64_t n = rows * cols;
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148LL * 16);
+  if (dtype == NKL_FLOAT32)
+    add_scalar_kernel<float><<<blocks, 256, 0, st>>>(static_cast<const float*>(x), static_cast<const float*>(residual),
+                                                     static_cast<float*>(sum_out), n);
+  else
+    add_scalar_kernel<bf16><<<blocks, 256, 0, st>>>(static_cast<const bf16*>(x), static_cast<const bf16*>(residual),
+                                                    static_cast<bf16*>(sum_out), n);
+  rc = check_launch("nkl_add_rmsnorm");
+  if (rc) return rc;
+  return dtype == NKL_FLOAT32 ? rmsnorm_launch<float>(sum_out, weight, out, rows, cols, eps, st)
+                              : rmsnorm_launch<bf16>(sum_out, weight, out, rows, cols, eps, st);
 }
 
 extern "C" int nkl_softmax(const void* x, void* out, int64_t rows, int64_t cols, int dtype, void* stream) {

@@ -38,6 +38,7 @@ SIGNATURES = {
     "nkl_last_error": (ctypes.c_char_p, []),
     "nkl_check_device": (_int, [_p]),
     "nkl_rmsnorm": (_int, [_p, _p, _p, _i64, _i64, _f, _int, _p]),
+    "nkl_add_rmsnorm": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _f, _int, _p]),
     "nkl_softmax": (_int, [_p, _p, _i64, _i64, _int, _p]),
     "nkl_softmax_unfused_workspace_size": (_sz, [_i64, _i64]),
     "nkl_softmax_unfused": (_int, [_p, _p, _p, _sz, _i64, _i64, _int, _p]),

@@ -121,6 +121,28 @@ def _(a, b, naive):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
+@torch.library.custom_op("nkilab::add_rmsnorm", mutates_args=())
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, weight: torch.Tensor,
+                eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    """(x + residual rounded to x.dtype, rmsnorm of that sum) in one pass."""
+    dev, dt, st = _prep(x, residual, weight)
+    if residual.shape != x.shape:
+        raise ValueError(f"x {tuple(x.shape)} and residual {tuple(residual.shape)} must match")
+    cols = x.shape[-1]
+    rows = x.numel() // cols if cols else 0
+    s = torch.empty_like(x)
+    out = torch.empty_like(x)
+    with torch.cuda.device(dev):
+        N.call("nkl_add_rmsnorm", x.data_ptr(), residual.data_ptr(), weight.data_ptr(), s.data_ptr(), out.data_ptr(),
+               rows, cols, eps, dt, st)
+    return s, out
+
+
+@add_rmsnorm.register_fake
+def _(x, residual, weight, eps):
+    return torch.empty_like(x), torch.empty_like(x)
+
+
 @torch.library.custom_op("nkilab::rope", mutates_args=())
 def rope(x: torch.Tensor, base: float, pos_offset: int) -> torch.Tensor:
     """Rotary position embedding (rotate-half) of x [heads, seq, head_dim]."""

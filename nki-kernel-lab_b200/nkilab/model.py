@@ -118,8 +118,8 @@ def _forward_device(block: DecoderBlock, x: torch.Tensor, attention_variant: str
     q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).reshape(B * H, S, hd) for i in range(3))
     a = ops.attention(q, k, v, variant=attention_variant)
     a = a.view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B * S, d)
-    x2 = x2 + ops.matmul(a, w["wo"])
-    h = ops.rmsnorm(x2, w["norm2"], cfg.eps)
+    # residual add fused with the second RMSNorm (same rounding as add-then-norm)
+    x2, h = torch.ops.nkilab.add_rmsnorm(x2.contiguous(), ops.matmul(a, w["wo"]).contiguous(), w["norm2"], cfg.eps)
     if "wgu" in w:
         act = torch.ops.nkilab.matmul_swiglu(h.contiguous(), w["wgu"])
     else:

@@ -230,3 +230,20 @@ def test_rope_in_place_and_bad_shapes():
     assert torch.equal(x, want)
     assert N.lib.nkl_rope(x.data_ptr(), x.data_ptr(), 2, 64, 120, 10000.0, 0, N.BFLOAT16, st) == N.ERR_SHAPE
     assert N.lib.nkl_rope(x.data_ptr(), x.data_ptr(), 2, 64, 128, 1.0, 0, N.BFLOAT16, st) == N.ERR_ARG
+
+
+@pytest.mark.parametrize("rows,cols,dt", [(4096, 2048, torch.bfloat16), (300, 777, torch.bfloat16),
+                                          (64, 1024, torch.float32), (5, 24, torch.float32)])
+def test_add_rmsnorm_equals_add_then_norm(rows, cols, dt):
+    """The fused residual add + RMSNorm returns exactly what the add (rounded to the dtype)
+    followed by nkl_rmsnorm returns, for the vectorised and the two-pass shapes."""
+    from nkilab import ops
+
+    g = torch.Generator().manual_seed(rows + cols)
+    x = torch.randn(rows, cols, generator=g).to(dt).cuda()
+    r = torch.randn(rows, cols, generator=g).to(dt).cuda()
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).to(dt).cuda()
+    s, y = torch.ops.nkilab.add_rmsnorm(x, r, w, 1e-6)
+    s_ref = x + r
+    assert torch.equal(s, s_ref)
+    assert torch.equal(y, ops.rmsnorm(s_ref, w, 1e-6))
