@@ -8,9 +8,10 @@
 // The reference tiles 128 rows onto SBUF partitions; on B200 a row maps to one warp
 // (rows up to 512 16-byte vectors) held entirely in registers, so every byte of the
 // input is read from HBM once and every output byte written once, with 16-byte
-// coalesced accesses. A warp owns RPW consecutive rows and issues every load of all
-// of them before the first reduction, which keeps 16 KiB per warp in flight; kernels
-// are launched with programmatic dependent launch (launch_pdl). Rows that are too long
+// coalesced accesses. A warp issues every load of its row before the first reduction,
+// and the launch shapes keep enough warps resident that (at the benchmark shape) every
+// row is in flight at once; kernels are launched with programmatic dependent launch
+// (launch_pdl). Rows that are too long
 // or not 16-byte aligned fall back to a block-per-row kernel that streams the row more
 // than once (still exact).
 //
@@ -26,61 +27,78 @@
 namespace nkl {
 namespace {
 
-// Launch shapes (rows of up to 64 16-byte vectors per lane), chosen by measurement on
-// B200 at [4096, 2048] bf16: RMSNorm holds two rows per warp in flight; softmax keeps
-// one row per warp (its exponentials stay in registers).
-constexpr int kRmsWarpsPerBlock = 2, kRmsRowsPerWarp = 2;
-constexpr int kSoftmaxWarpsPerBlock = 4, kSoftmaxRowsPerWarp = 1;
+// Launch shapes, chosen by measurement on B200 at [4096, 2048] bf16 (4096 rows, one
+// warp each). A warp holds its row in registers from the first load to the last store,
+// so the number of rows in flight is the number of resident warps: RMSNorm is capped at
+// 72 registers (7 four-warp blocks, 28 warps per SM), which puts all 4096 rows on the
+// GPU in one wave; softmax keeps its 64 exponentials in registers (about 80 registers,
+// 24 warps per SM) and runs two-warp blocks, which fill the last partial wave at the
+// finest grain.
+constexpr int kRmsWarpsPerBlock = 4;
+// Resident four-warp blocks per SM that the register cap allows: 7 (72 registers) for rows
+// of up to 8 vectors per lane, 4 (128 registers) for the 16-vector rows.
+constexpr int rms_min_blocks(int nv) { return nv <= 8 ? 7 : 4; }
+// The fused residual add holds two rows (x and the residual) while its loads are in flight;
+// two-warp blocks without a register cap measured fastest for it.
+constexpr int kAddRmsWarpsPerBlock = 2;
+constexpr int kSoftmaxWarpsPerBlock = 2;
 constexpr int kMaxVecPerLane = 16;  // 512 vectors per row: 4096 bf16 / 2048 fp32 columns
+
+// Element e of a 16-byte vector as fp32, with `z` (zero at run time) folded into the bit
+// pattern. The fold costs nothing (the bf16 unpack is an integer op either way) but makes
+// the value depend on whatever produced z: a pass that unpacks a row a second time after
+// a reduction ties its unpacks to the reduction's result, so the compiler keeps only the
+// packed row (4 registers per vector) live across the reduction instead of hoisting the
+// unpacked fp32 values (8 per vector) above it.
+template <typename T> __device__ __forceinline__ float vec_get_tied(const Vec16<T>& v, int e, uint32_t z) {
+  if constexpr (sizeof(T) == 4) {
+    return reinterpret_cast<const float*>(&v.raw)[e];
+  } else {
+    const uint32_t w = reinterpret_cast<const uint32_t*>(&v.raw)[e >> 1];
+    return __uint_as_float((e & 1) ? ((w & 0xffff0000u) | z) : (w * 65536u + z));
+  }
+}
 
 // ------------------------------------------------------------------ RMSNorm
 
-template <typename T, int NV, int RPW>
-__global__ void __launch_bounds__(kRmsWarpsPerBlock * 32)
+// FULL: the row fills every lane's NV vectors (cols == 32 * NV * V), so no column guards.
+template <typename T, int NV, bool FULL>
+__global__ void __launch_bounds__(kRmsWarpsPerBlock * 32, rms_min_blocks(NV))
 rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int64_t rows, int cols,
                     float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
   pdl_enter();
-  const int64_t row0 = ((int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5)) * RPW;
+  const int64_t row = (int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row0 >= rows) return;
+  if (row >= rows) return;
   const int nvec = cols / V;
-  Vec16<T> xv[RPW][NV];
+  const T* xr = x + row * cols;
+  Vec16<T> xv[NV];
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = i * 32 + lane;
-      if (row0 + r < rows && j < nvec) xv[r][i].raw = ld_stream(x + (row0 + r) * cols + (int64_t)j * V);
-      else xv[r][i].raw = make_uint4(0u, 0u, 0u, 0u);
-    }
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    xv[i].raw = (FULL || j < nvec) ? ld_stream(xr + j * V) : make_uint4(0u, 0u, 0u, 0u);
   }
+  // Four partial sums break the dependent chain of NV * V fused multiply-adds.
+  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    if (row0 + r >= rows) break;
-    float ssq = 0.f;
+  for (int i = 0; i < NV; ++i) {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
+    for (int e = 0; e < V; ++e) { const float f = xv[i].get(e); ssq[e & 3] = fmaf(f, f, ssq[e & 3]); }
+  }
+  const float rstd = rsqrtf(warp_sum((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) * inv_cols + eps);
+  const uint32_t z = __float_as_uint(rstd) >> 31;  // rstd > 0: zero, and tied to the reduction
+  T* yr = y + row * cols;
 #pragma unroll
-      for (int e = 0; e < V; ++e) { const float f = xv[r][i].get(e); ssq += f * f; }
-    }
-    ssq = warp_sum(ssq);
-    const float rstd = rsqrtf(ssq * inv_cols + eps);
-    T* yr = y + (row0 + r) * cols;
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (FULL || j < nvec) {
+      Vec16<T> wv;
+      wv.raw = *reinterpret_cast<const uint4*>(w + j * V + z);
+      float o[V];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = i * 32 + lane;
-      if (j < nvec) {
-        Vec16<T> wv;
-        wv.raw = __ldg(reinterpret_cast<const uint4*>(w + (int64_t)j * V));
-        float o[V];
-#pragma unroll
-        for (int e = 0; e < V; ++e) {
-          const float xn = xv[r][i].get(e) * rstd;  // fp32 x * rstd, then * weight
-          o[e] = xn * wv.get(e);
-        }
-        st_stream(yr + (int64_t)j * V, pack16<T>(o));
-      }
+      for (int e = 0; e < V; ++e) o[e] = (vec_get_tied(xv[i], e, z) * rstd) * wv.get(e);  // fp32 x * rstd, then * weight
+      st_stream(yr + j * V, pack16<T>(o));
     }
   }
 }
@@ -125,66 +143,79 @@ rmsnorm_block_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __rest
 
 // ------------------------------------------------------------------ fused softmax
 
-template <typename T, int NV, int RPW>
+// exp(x - max) for the fused softmax. fp32 outputs use the accurate library expf (the
+// reference's fp32 tolerance is 1e-5). bf16 outputs use exp(t) = 2^(t * log2(e)) with the
+// argument formed by one fused multiply-add, x * log2(e) + (-max * log2(e)), and the
+// hardware base-2 exponential (ex2.approx.ftz: relative error about 2^-22, far below one
+// bf16 ulp; results under 2^-126 flush to zero, where the rounded bf16 output is zero or
+// subnormal anyway).
+constexpr float kLog2e = 1.4426950408889634f;
+__device__ __forceinline__ float ex2_approx_ftz(float t) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(t));
+  return r;
+}
+template <typename T> __device__ __forceinline__ float softmax_exp(float x, float mx, float neg_mx_log2e) {
+  if constexpr (sizeof(T) == 4) return expf(x - mx);
+  else return ex2_approx_ftz(fmaf(x, kLog2e, neg_mx_log2e));
+}
+
+template <typename T, int NV, bool FULL>
 __global__ void __launch_bounds__(kSoftmaxWarpsPerBlock * 32)
 softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols) {
   constexpr int V = Vec16<T>::N;
   pdl_enter();
-  const int64_t row0 = ((int64_t)blockIdx.x * kSoftmaxWarpsPerBlock + (threadIdx.x >> 5)) * RPW;
+  const int64_t row = (int64_t)blockIdx.x * kSoftmaxWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (row0 >= rows) return;
+  if (row >= rows) return;
   const int nvec = cols / V;
-  Vec16<T> xv[RPW][NV];
+  const T* xr = x + row * cols;
+  Vec16<T> xv[NV];
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (FULL || j < nvec) xv[i].raw = ld_stream(xr + j * V);
+  }
+  // Four partial maxima / sums break the dependent chains of NV * V operations.
+  float m[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = i * 32 + lane;
-      if (row0 + r < rows && j < nvec) xv[r][i].raw = ld_stream(x + (row0 + r) * cols + (int64_t)j * V);
+  for (int i = 0; i < NV; ++i) {
+    if (FULL || i * 32 + lane < nvec) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) m[e & 3] = fmaxf(m[e & 3], xv[i].get(e));
     }
   }
+  const float mx = warp_max(fmaxf(fmaxf(m[0], m[1]), fmaxf(m[2], m[3])));
+  const float neg_mx_log2e = -mx * kLog2e;
   // Rows of up to 64 values per lane keep exp(x - max) in registers, so each element
   // costs one exp; longer rows recompute it in the output pass to bound registers.
   constexpr bool kKeep = NV * V <= 64;
+  float ex[kKeep ? NV * V : 1];
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-  for (int r = 0; r < RPW; ++r) {
-    if (row0 + r >= rows) break;
-    float m = -INFINITY;
+  for (int i = 0; i < NV; ++i) {
+    if (FULL || i * 32 + lane < nvec) {
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane < nvec) {
-#pragma unroll
-        for (int e = 0; e < V; ++e) m = fmaxf(m, xv[r][i].get(e));
+      for (int e = 0; e < V; ++e) {
+        const float t = softmax_exp<T>(xv[i].get(e), mx, neg_mx_log2e);
+        if constexpr (kKeep) ex[i * V + e] = t;
+        s[e & 3] += t;
       }
     }
-    const float neg_max = -warp_max(m);
-    float ex[kKeep ? NV * V : 1];
-    float s = 0.f;
+  }
+  const float rinv = 1.0f / warp_sum((s[0] + s[1]) + (s[2] + s[3]));
+  T* yr = y + row * cols;
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if (i * 32 + lane < nvec) {
+  for (int i = 0; i < NV; ++i) {
+    const int j = i * 32 + lane;
+    if (FULL || j < nvec) {
+      float o[V];
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-          const float t = row_exp<T>(xv[r][i].get(e) + neg_max);
-          if constexpr (kKeep) ex[i * V + e] = t;
-          s += t;
-        }
+      for (int e = 0; e < V; ++e) {
+        if constexpr (kKeep) o[e] = ex[i * V + e] * rinv;
+        else o[e] = softmax_exp<T>(xv[i].get(e), mx, neg_mx_log2e) * rinv;
       }
-    }
-    const float rinv = 1.0f / warp_sum(s);
-    T* yr = y + (row0 + r) * cols;
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      const int j = i * 32 + lane;
-      if (j < nvec) {
-        float o[V];
-#pragma unroll
-        for (int e = 0; e < V; ++e) {
-          if constexpr (kKeep) o[e] = ex[i * V + e] * rinv;
-          else o[e] = row_exp<T>(xv[r][i].get(e) + neg_max) * rinv;
-        }
-        st_stream(yr + (int64_t)j * V, pack16<T>(o));
-      }
+      st_stream(yr + j * V, pack16<T>(o));
     }
   }
 }
@@ -302,12 +333,12 @@ swiglu_scalar_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __rest
 // nkilab/model.py:86,89), written out, then y = rmsnorm(s) with the same rounding points
 // as rmsnorm_warp_kernel: one pass over x and r instead of an add kernel and a norm kernel.
 template <typename T, int NV>
-__global__ void __launch_bounds__(kRmsWarpsPerBlock * 32)
+__global__ void __launch_bounds__(kAddRmsWarpsPerBlock * 32)
 add_rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
                         T* __restrict__ s_out, T* __restrict__ y, int64_t rows, int cols, float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
   pdl_enter();
-  const int64_t row = (int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5);
+  const int64_t row = (int64_t)blockIdx.x * kAddRmsWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   const int nvec = cols / V;
@@ -334,14 +365,15 @@ add_rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ res, cons
       if (j < nvec) st_stream(s_out + row * cols + (int64_t)j * V, sv[i].raw);
     }
   }
-  float ssq = 0.f;
+  // The same partial sums in the same order as rmsnorm_warp_kernel, so the result equals
+  // rmsnorm(x + residual) bit for bit.
+  float ssq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
 #pragma unroll
-    for (int e = 0; e < V; ++e) { const float f = sv[i].get(e); ssq += f * f; }
+    for (int e = 0; e < V; ++e) { const float f = sv[i].get(e); ssq[e & 3] = fmaf(f, f, ssq[e & 3]); }
   }
-  ssq = warp_sum(ssq);
-  const float rstd = rsqrtf(ssq * inv_cols + eps);
+  const float rstd = rsqrtf(warp_sum((ssq[0] + ssq[1]) + (ssq[2] + ssq[3])) * inv_cols + eps);
   T* yr = y + row * cols;
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
@@ -428,18 +460,18 @@ int rmsnorm_launch(const void* x, const void* w, void* y, int64_t rows, int64_t 
   const T* wp = static_cast<const T*>(w);
   T* yp = static_cast<T*>(y);
   if (row_vectorizable<T>(cols, x, y, w)) {
-    const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
+    const int64_t nvec = cols / (16 / (int64_t)sizeof(T));
+    const int nv = nv_bucket(nvec);
+    const bool full = nvec == 32 * (int64_t)nv;
     const int c = (int)cols;
-    const dim3 blk(kRmsWarpsPerBlock * 32);
-    auto grid = [&](int rpw) {
-      return dim3((unsigned)((rows + (int64_t)kRmsWarpsPerBlock * rpw - 1) / ((int64_t)kRmsWarpsPerBlock * rpw)));
-    };
+    const dim3 grid((unsigned)((rows + kRmsWarpsPerBlock - 1) / kRmsWarpsPerBlock)), blk(kRmsWarpsPerBlock * 32);
+    auto go = [&](auto kernel) { return launch_pdl(kernel, grid, blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps); };
     switch (nv) {
-      case 1: return launch_pdl(rmsnorm_warp_kernel<T, 1, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
-      case 2: return launch_pdl(rmsnorm_warp_kernel<T, 2, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
-      case 4: return launch_pdl(rmsnorm_warp_kernel<T, 4, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
-      case 8: return launch_pdl(rmsnorm_warp_kernel<T, 8, kRmsRowsPerWarp>, grid(kRmsRowsPerWarp), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
-      default: return launch_pdl(rmsnorm_warp_kernel<T, 16, 1>, grid(1), blk, 0, st, "nkl_rmsnorm", xp, wp, yp, rows, c, inv_cols, eps);
+      case 1: return full ? go(rmsnorm_warp_kernel<T, 1, true>) : go(rmsnorm_warp_kernel<T, 1, false>);
+      case 2: return full ? go(rmsnorm_warp_kernel<T, 2, true>) : go(rmsnorm_warp_kernel<T, 2, false>);
+      case 4: return full ? go(rmsnorm_warp_kernel<T, 4, true>) : go(rmsnorm_warp_kernel<T, 4, false>);
+      case 8: return full ? go(rmsnorm_warp_kernel<T, 8, true>) : go(rmsnorm_warp_kernel<T, 8, false>);
+      default: return full ? go(rmsnorm_warp_kernel<T, 16, true>) : go(rmsnorm_warp_kernel<T, 16, false>);
     }
   } else {
     rmsnorm_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, wp, yp, rows, cols, inv_cols, eps);
@@ -452,19 +484,18 @@ int softmax_launch(const void* x, void* y, int64_t rows, int64_t cols, cudaStrea
   const T* xp = static_cast<const T*>(x);
   T* yp = static_cast<T*>(y);
   if (row_vectorizable<T>(cols, x, y, nullptr)) {
-    const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
+    const int64_t nvec = cols / (16 / (int64_t)sizeof(T));
+    const int nv = nv_bucket(nvec);
+    const bool full = nvec == 32 * (int64_t)nv;
     const int c = (int)cols;
-    const dim3 blk(kSoftmaxWarpsPerBlock * 32);
-    auto grid = [&](int rpw) {
-      return dim3(
-          (unsigned)((rows + (int64_t)kSoftmaxWarpsPerBlock * rpw - 1) / ((int64_t)kSoftmaxWarpsPerBlock * rpw)));
-    };
+    const dim3 grid((unsigned)((rows + kSoftmaxWarpsPerBlock - 1) / kSoftmaxWarpsPerBlock)), blk(kSoftmaxWarpsPerBlock * 32);
+    auto go = [&](auto kernel) { return launch_pdl(kernel, grid, blk, 0, st, "nkl_softmax", xp, yp, rows, c); };
     switch (nv) {
-      case 1: return launch_pdl(softmax_warp_kernel<T, 1, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
-      case 2: return launch_pdl(softmax_warp_kernel<T, 2, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
-      case 4: return launch_pdl(softmax_warp_kernel<T, 4, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
-      case 8: return launch_pdl(softmax_warp_kernel<T, 8, kSoftmaxRowsPerWarp>, grid(kSoftmaxRowsPerWarp), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
-      default: return launch_pdl(softmax_warp_kernel<T, 16, 1>, grid(1), blk, 0, st, "nkl_softmax", xp, yp, rows, c);
+      case 1: return full ? go(softmax_warp_kernel<T, 1, true>) : go(softmax_warp_kernel<T, 1, false>);
+      case 2: return full ? go(softmax_warp_kernel<T, 2, true>) : go(softmax_warp_kernel<T, 2, false>);
+      case 4: return full ? go(softmax_warp_kernel<T, 4, true>) : go(softmax_warp_kernel<T, 4, false>);
+      case 8: return full ? go(softmax_warp_kernel<T, 8, true>) : go(softmax_warp_kernel<T, 8, false>);
+      default: return full ? go(softmax_warp_kernel<T, 16, true>) : go(softmax_warp_kernel<T, 16, false>);
     }
   } else {
     softmax_block_kernel<T><<<(unsigned)rows, 256, 0, st>>>(xp, yp, rows, cols);
@@ -542,7 +573,7 @@ extern "C" int nkl_add_rmsnorm(const void* x, const void* residual, const void* 
   auto fused = [&](auto tag) -> int {
     using T = decltype(tag);
     const int nv = nv_bucket(cols / (16 / (int64_t)sizeof(T)));
-    const dim3 grid((unsigned)((rows + kRmsWarpsPerBlock - 1) / kRmsWarpsPerBlock)), blk(kRmsWarpsPerBlock * 32);
+    const dim3 grid((unsigned)((rows + kAddRmsWarpsPerBlock - 1) / kAddRmsWarpsPerBlock)), blk(kAddRmsWarpsPerBlock * 32);
     const T* xp = static_cast<const T*>(x);
     const T* rp = static_cast<const T*>(residual);
     const T* wp = static_cast<const T*>(weight);
