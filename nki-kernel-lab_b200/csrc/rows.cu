@@ -664,7 +664,7 @@ extern "C" int nkl_swiglu(const void* gate, const void* up, void* out, int64_t r
 namespace nkl {
 namespace {
 
-__device__ __align__(256) unsigned char g_softmax_static_scratch[NKL_SOFTMAX_UNFUSED_STATIC_BYTES];
+static __device__ __align__(256) unsigned char g_softmax_static_scratch[NKL_SOFTMAX_UNFUSED_STATIC_BYTES];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_static_scratch_mu;
