@@ -161,14 +161,33 @@ struct AttnArgs {
   int kv_group;  // query heads per key/value head (1 = multi-head, heads = multi-query)
   float scale_log2;
   size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (max, sum) and O regions
-  int n_ctas_listed;              // > 0: cta_off / unit_list give each CTA's units
+  int n_ctas_listed;              // > 0: cta_off / unit_desc give each CTA's units
   uint16_t cta_off[kMaxCtas + 1];
-  uint16_t unit_list[kMaxSched];
+  // Units decoded on the host, packed in two words:
+  //   a = unit (10 bits) | head << 10 (11 bits) | kv head << 21 (11 bits)
+  //   b = query tile (11 bits) | first key tile << 11 (11 bits) | (key tiles - 1) << 22
+  // (listed plans have at most kMaxSched = 1024 units, so every field fits). Decoding on
+  // the device would cost a chain of integer divisions per unit, and on sm_100 those issue
+  // on the MUFU pipe that the softmax warps keep saturated with ex2: the producer and
+  // MMA warps stalled ~2 us at every unit boundary behind them.
+  uint2 unit_desc[kMaxSched];
 };
 
 struct Unit {
   int head, qt, chunk, n_chunks, j0, n, v0;  // v0: per-head index of this query tile's chunk 0
 };
+
+// What the kernel needs of a unit: its index (workspace slot), heads, query tile and key
+// tile range; split = the unit covers only part of its query tile's causal key range.
+struct UnitRun {
+  int u, head, kv_head, qt, j0, n;
+  bool split;
+};
+
+__host__ __device__ __forceinline__ uint2 pack_unit(int u, int head, int kv_head, int qt, int j0, int n) {
+  return make_uint2((uint32_t)u | ((uint32_t)head << 10) | ((uint32_t)kv_head << 21),
+                    (uint32_t)qt | ((uint32_t)j0 << 11) | ((uint32_t)(n - 1) << 22));
+}
 
 // Unit index -> (head, query tile, chunk). Units run head-fastest; query tiles longest
 // (latest) first; chunks of C key tiles ascending.
@@ -211,15 +230,31 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, volati
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-__device__ __forceinline__ int unit_of(const AttnArgs& a, int i, int& u) {
+// The i-th unit of this CTA: from the host-decoded list, or (plans too large to list)
+// round-robin over CTAs, decoded here once per unit.
+__device__ __forceinline__ bool next_unit(const AttnArgs& a, int i, UnitRun& r) {
   if (a.n_ctas_listed > 0) {
     const int k = a.cta_off[blockIdx.x] + i;
-    if (k >= a.cta_off[blockIdx.x + 1]) return 0;
-    u = a.unit_list[k];
-    return 1;
+    if (k >= a.cta_off[blockIdx.x + 1]) return false;
+    const uint2 d = a.unit_desc[k];
+    r.u = (int)(d.x & 1023u);
+    r.head = (int)((d.x >> 10) & 2047u);
+    r.kv_head = (int)(d.x >> 21);
+    r.qt = (int)(d.y & 2047u);
+    r.j0 = (int)((d.y >> 11) & 2047u);
+    r.n = (int)(d.y >> 22) + 1;
+  } else {
+    r.u = (int)blockIdx.x + i * (int)gridDim.x;
+    if (r.u >= a.units) return false;
+    const Unit un = decode_unit(r.u, a.heads, a.q_tiles, a.chunk);
+    r.head = un.head;
+    r.kv_head = un.head / a.kv_group;
+    r.qt = un.qt;
+    r.j0 = un.j0;
+    r.n = un.n;
   }
-  u = (int)blockIdx.x + i * (int)gridDim.x;
-  return u < a.units;
+  r.split = !(r.j0 == 0 && r.n == r.qt + 1);
+  return true;
 }
 
 template <int D>
@@ -245,7 +280,6 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int heads = args.heads, q_tiles = args.q_tiles;
   const float scale_log2 = args.scale_log2;
 
   if (threadIdx.x == 0) {
@@ -285,34 +319,33 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       uint32_t kc = 0, vc = 0, qc = 0;
       int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1}, q_armed[2] = {-1, -1};
       bool ok = true;
-      int u;
-      auto load_k = [&](const Unit& un, int t) -> bool {
+      UnitRun un;
+      // Key / value tile `kt` (absolute key-tile index) of kv head `kvh`.
+      auto load_k = [&](int kt, int kvh) -> bool {
         const int ks = kc & 1;
         if (!mbar_wait(&s.k_empty[ks], ((kc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 11)) return false;
         mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
         k_armed[ks] = (int)((kc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, (un.j0 + t) * kTile,
-                      un.head / args.kv_group);
+          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, kt * kTile, kvh);
         ++kc;
         return true;
       };
-      auto load_v = [&](const Unit& un, int t) -> bool {
+      auto load_v = [&](int kt, int kvh) -> bool {
         const int vs = vc & 1;
         if (!mbar_wait(&s.v_empty[vs], ((vc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 12)) return false;
         mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
         v_armed[vs] = (int)((vc >> 1) & 1u);
         for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, (un.j0 + t) * kTile,
-                      un.head / args.kv_group);
+          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, kt * kTile, kvh);
         ++vc;
         return true;
       };
       // Per unit, in the order the MMA warp consumes them: K(0), Q, K(1), then V(t)
       // followed by K(t+2).
-      for (int i = 0; ok && unit_of(args, i, u); ++i) {
-        const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
-        ok = load_k(un, 0);
+      for (int i = 0; ok && next_unit(args, i, un); ++i) {
+        const int j0 = un.j0, kvh = un.kv_head;
+        ok = load_k(j0, kvh);
         if (ok) {
           const int qb = qc & 1;
           if (!mbar_wait(&s.q_empty[qb], ((qc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) {
@@ -325,10 +358,10 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
             tma_load_3d(s.q[qb] + c * (kTile * 128), &map_q, &s.q_full[qb], c * 64, un.qt * kTile, un.head);
           ++qc;
         }
-        if (ok && un.n > 1) ok = load_k(un, 1);
+        if (ok && un.n > 1) ok = load_k(j0 + 1, kvh);
         for (int t = 0; ok && t < un.n; ++t) {
-          ok = load_v(un, t);
-          if (ok && t + 2 < un.n) ok = load_k(un, t + 2);
+          ok = load_v(j0 + t, kvh);
+          if (ok && t + 2 < un.n) ok = load_k(j0 + t + 2, kvh);
         }
       }
       if (!ok) {  // let issued copies land before shared memory is released
@@ -366,9 +399,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         }
         mma_commit(&s.s_full[b]);
       };
-      int u;
-      for (int i = 0; ok && unit_of(args, i, u); ++i) {
-        const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
+      UnitRun un;
+      for (int i = 0; ok && next_unit(args, i, un); ++i) {
         const int n = un.n;
         const int qb = qc & 1;
         if (!mbar_wait(&s.q_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
@@ -435,9 +467,9 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     const bool lead = threadIdx.x == 0;  // issues the output stores and frees the Q buffer
     uint32_t gt = 0, uc = 0, xc = 0;
     bool ok = true;
-    int u;
-    for (int i = 0; ok && unit_of(args, i, u); ++i) {
-      const Unit un = decode_unit(u, heads, q_tiles, args.chunk);
+    UnitRun un;
+    for (int i = 0; ok && next_unit(args, i, un); ++i) {
+      const int u = un.u;
       const int qt = un.qt;
       float m_ref = -INFINITY, l = 0.f;  // l: this half's share of the row sum
       for (int t = 0; t < un.n; ++t) {
@@ -511,7 +543,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       const float lt = s.xsum[r] + s.xsum[kTile + r];
       const float linv = 1.0f / lt;
       const int qb = uc & 1;  // this unit's Q buffer
-      if (un.n_chunks > 1) {
+      if (un.split) {
         // Split query tile: this chunk's O / sum in fp16 (a weighted mean of V rows,
         // rounded 2^-11 relative, far below the bf16 output's 2^-8) and its (max, sum);
         // attn_combine_bf16_kernel merges the chunks once this kernel has completed.
@@ -843,7 +875,8 @@ inline size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
 struct AttnPlan {
   int q_tiles = 0, chunk = 0, units = 0, ctas = 0;
   size_t stats_off = 0, o_off = 0, ws_bytes = 0;  // ws_bytes == 0: no split, no workspace
-  std::vector<uint16_t> cta_off, unit_list;       // empty: round-robin over CTAs
+  std::vector<uint16_t> cta_off;                  // empty: round-robin over CTAs
+  std::vector<uint2> unit_desc;                   // per listed unit, in cta_off order
   std::vector<CombineJob> jobs;                   // split query tiles (one job per tile, all heads)
 };
 
@@ -857,7 +890,7 @@ constexpr long kCombineCost = 6;
 
 // Longest-processing-time assignment of units to `ctas` CTAs; returns the makespan and
 // (optionally) fills the per-CTA lists.
-inline long lpt_schedule(int heads, int q_tiles, int C, int units, int ctas, AttnPlan* out) {
+inline long lpt_schedule(int heads, int q_tiles, int C, int units, int ctas, int kv_group, AttnPlan* out) {
   std::vector<std::pair<int, int>> cost(units);  // (cost, unit)
   for (int u = 0; u < units; ++u) cost[u] = {unit_cost(decode_unit(u, heads, q_tiles, C)), u};
   std::stable_sort(cost.begin(), cost.end(), [](const std::pair<int, int>& a, const std::pair<int, int>& b) {
@@ -874,10 +907,13 @@ inline long lpt_schedule(int heads, int q_tiles, int C, int units, int ctas, Att
   }
   if (out) {
     out->cta_off.assign(1, 0);
-    out->unit_list.clear();
+    out->unit_desc.clear();
     for (int b = 0; b < ctas; ++b) {
-      out->unit_list.insert(out->unit_list.end(), lists[b].begin(), lists[b].end());
-      out->cta_off.push_back((uint16_t)out->unit_list.size());
+      for (const uint16_t u : lists[b]) {
+        const Unit un = decode_unit(u, heads, q_tiles, C);
+        out->unit_desc.push_back(pack_unit(u, un.head, un.head / kv_group, un.qt, un.j0, un.n));
+      }
+      out->cta_off.push_back((uint16_t)out->unit_desc.size());
     }
   }
   return *std::max_element(load.begin(), load.end());
@@ -889,7 +925,7 @@ inline long count_units(int heads, int q_tiles, int C) {
   return (long)heads * per_head;
 }
 
-AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
+AttnPlan plan_attention(int heads, int kv_group, int seq, int d, bool allow_split, int sms) {
   AttnPlan p;
   p.q_tiles = (seq + kTile - 1) / kTile;
   const int max_nt = p.q_tiles;
@@ -903,7 +939,7 @@ AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
     const long units = count_units(heads, p.q_tiles, C);
     if (units > kMaxSched) break;
     const int ctas = (int)std::min<long>(units, sms);
-    const long span = lpt_schedule(heads, p.q_tiles, C, (int)units, ctas, nullptr) + (C < max_nt ? kCombineCost : 0);
+    const long span = lpt_schedule(heads, p.q_tiles, C, (int)units, ctas, kv_group, nullptr) + (C < max_nt ? kCombineCost : 0);
     if (best_span < 0 || span < best_span) {
       best_span = span;
       best_c = C;
@@ -913,7 +949,7 @@ AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
   const long units = count_units(heads, p.q_tiles, p.chunk);
   p.units = (int)std::min<long>(units, 1L << 30);
   p.ctas = (int)std::min<long>(units, sms);
-  if (units <= kMaxSched && p.ctas <= kMaxCtas) lpt_schedule(heads, p.q_tiles, p.chunk, p.units, p.ctas, &p);
+  if (units <= kMaxSched && p.ctas <= kMaxCtas) lpt_schedule(heads, p.q_tiles, p.chunk, p.units, p.ctas, kv_group, &p);
   if (p.chunk < max_nt) {
     p.stats_off = 0;
     p.o_off = round256((size_t)p.units * 2 * kTile * sizeof(float));
@@ -935,15 +971,15 @@ AttnPlan plan_attention(int heads, int seq, int d, bool allow_split, int sms) {
   return p;
 }
 
-// Plans are cached per (heads, seq, d, split, SMs); the LPT search costs a few ms.
-const AttnPlan& cached_plan(int heads, int seq, int d, bool allow_split) {
+// Plans are cached per (heads, kv group, seq, d, split, SMs); the LPT search costs a few ms.
+const AttnPlan& cached_plan(int heads, int kv_group, int seq, int d, bool allow_split) {
   static std::mutex mu;
-  static std::map<std::tuple<int, int, int, bool, int>, AttnPlan> cache;
+  static std::map<std::tuple<int, int, int, int, bool, int>, AttnPlan> cache;
   const int sms = sm_count();
   std::lock_guard<std::mutex> lock(mu);
-  auto key = std::make_tuple(heads, seq, d, allow_split, sms);
+  auto key = std::make_tuple(heads, kv_group, seq, d, allow_split, sms);
   auto it = cache.find(key);
-  if (it == cache.end()) it = cache.emplace(key, plan_attention(heads, seq, d, allow_split, sms)).first;
+  if (it == cache.end()) it = cache.emplace(key, plan_attention(heads, kv_group, seq, d, allow_split, sms)).first;
   return it->second;
 }
 
@@ -956,7 +992,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, "nkl_attention(v)");
   if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, "nkl_attention(out)");
   if (rc) return rc;
-  const AttnPlan& plan = cached_plan(heads, seq, D, ws != nullptr);
+  const AttnPlan& plan = cached_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
     return fail(NKL_ERR_ARG, "nkl_attention_ws: workspace %zu B < required %zu B", ws_bytes, plan.ws_bytes);
   constexpr size_t smem = attn_smem_bytes<D>();
@@ -980,7 +1016,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   a.ws_o_off = plan.o_off;
   a.n_ctas_listed = plan.cta_off.empty() ? 0 : plan.ctas;
   for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
-  for (size_t i = 0; i < plan.unit_list.size(); ++i) a.unit_list[i] = plan.unit_list[i];
+  for (size_t i = 0; i < plan.unit_desc.size(); ++i) a.unit_desc[i] = plan.unit_desc[i];
   attn_fwd_bf16_kernel<D><<<plan.ctas, kAttnThreads, smem, st>>>(mq, mk, mv, mo, a);
   rc = check_launch("nkl_attention");
   if (rc || plan.jobs.empty()) return rc;
@@ -1069,7 +1105,7 @@ extern "C" int nkl_attention(const void* q, const void* k, const void* v, void* 
 extern "C" size_t nkl_attention_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype) {
   if (dtype != NKL_BFLOAT16 || heads <= 0 || seq <= 0 || (head_dim != 64 && head_dim != 128)) return 0;
   if (heads > 65535 || seq > (1 << 24)) return 0;
-  return cached_plan((int)heads, (int)seq, (int)head_dim, true).ws_bytes;
+  return cached_plan((int)heads, 1, (int)seq, (int)head_dim, true).ws_bytes;  // independent of the kv group
 }
 
 extern "C" int nkl_attention_ws(const void* q, const void* k, const void* v, void* out, void* workspace,
