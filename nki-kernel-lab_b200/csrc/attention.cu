@@ -312,6 +312,11 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // Launched with programmatic dependent launch: the prologue above (barriers, TMEM,
+  // descriptor prefetch) overlaps the previous kernel of the stream; nothing in global
+  // memory (q, k, v, the output, the workspace a previous combine kernel may still be
+  // reading) is touched before that kernel has completed and its writes are visible.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------ TMA producer
@@ -1017,8 +1022,8 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   a.n_ctas_listed = plan.cta_off.empty() ? 0 : plan.ctas;
   for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
   for (size_t i = 0; i < plan.unit_desc.size(); ++i) a.unit_desc[i] = plan.unit_desc[i];
-  attn_fwd_bf16_kernel<D><<<plan.ctas, kAttnThreads, smem, st>>>(mq, mk, mv, mo, a);
-  rc = check_launch("nkl_attention");
+  rc = launch_pdl(attn_fwd_bf16_kernel<D>, dim3(plan.ctas), dim3(kAttnThreads), smem, st, "nkl_attention", mq, mk, mv,
+                  mo, a);
   if (rc || plan.jobs.empty()) return rc;
   // split query tiles: merge the partials (programmatic dependent launch: the combine
   // grid is scheduled early and waits on the device for the attention grid)
