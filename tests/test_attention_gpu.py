@@ -195,3 +195,48 @@ def test_grouped_query_attention_rejects_bad_head_counts():
     rc = N.lib.nkl_attention_gqa(q.data_ptr(), kv.data_ptr(), kv.data_ptr(), q.data_ptr(), None, 0, 6, 4, 128, 64,
                                  0.125, N.BFLOAT16, st)
     assert rc == N.ERR_SHAPE and "kv_heads must divide heads" in N.lib.nkl_last_error().decode()
+
+
+def test_split_kv_workspace_under_cuda_graph_replay():
+    """The split path (attention kernel + combine kernel) captured once in a CUDA graph
+    and replayed on new inputs in the captured buffers: every replay matches an eager
+    nkl_attention_ws call on the same inputs bit for bit, and the oracle."""
+    import ctypes
+    import math
+
+    from nkilab import _native as N
+
+    H, S, D = 8, 2048, 128
+    g = torch.Generator().manual_seed(5)
+    q, k, v = (torch.empty(H, S, D, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    nbytes = N.lib.nkl_attention_workspace_size(H, S, D, N.BFLOAT16)
+    assert nbytes > 0
+    ws_graph = torch.full((nbytes,), 0x5A, dtype=torch.uint8, device="cuda")
+    ws_eager = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    o_graph, o_eager = torch.empty_like(q), torch.empty_like(q)
+    p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
+    scale = 1 / math.sqrt(D)
+
+    def call(o, ws):
+        st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+        return N.lib.nkl_attention_ws(p(q), p(k), p(v), p(o), p(ws), nbytes, H, S, D, scale, N.BFLOAT16, st)
+
+    for t in (q, k, v):
+        t.copy_(torch.randn(H, S, D, generator=g).to(torch.bfloat16))
+    assert call(o_graph, ws_graph) == N.OK  # plan and kernel attributes set up before capture
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=side):
+        assert call(o_graph, ws_graph) == N.OK
+    for trial in range(3):
+        for t in (q, k, v):
+            t.copy_(torch.randn(H, S, D, generator=g).to(torch.bfloat16))
+        o_graph.fill_(float("nan"))
+        graph.replay()
+        assert call(o_eager, ws_eager) == N.OK
+        torch.cuda.synchronize()
+        N.check_device(torch.cuda.current_stream().cuda_stream)
+        assert torch.equal(o_graph, o_eager), f"replay {trial}"
+    _check_vs_oracle(o_graph, q.cpu(), k.cpu(), v.cpu())
+
