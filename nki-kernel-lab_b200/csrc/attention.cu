@@ -63,7 +63,7 @@ constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 constexpr int kMaxCtas = 192;         // schedule table capacity (>= SMs of any sm_100 part)
 constexpr int kMaxSched = 1024;       // units listed explicitly; more units: round-robin
-constexpr int kMaxChunks = 4;         // a query tile's key range is split into at most 4 units
+constexpr int kMaxChunks = 8;         // a query tile's key range is split into at most 8 units
 
 __device__ __forceinline__ float fast_exp2(float x) {
   float y;
@@ -629,7 +629,9 @@ struct CombineArgs {
   CombineJob job[kMaxCombineJobs];
 };
 
-template <int D>
+// NC: chunk slots, the smallest of 2, 4, 8 covering the plan (unused slots add exact
+// zeros, so every NC gives the same bits).
+template <int D, int NC>
 __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_constant__ CombineArgs args) {
   pdl_enter();  // the attention grid before this one has completed and its partials are visible
   const CombineJob jb = args.job[blockIdx.x];
@@ -642,10 +644,10 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
   const size_t slot0 = (size_t)jb.v0 * args.heads + head;
   const float* stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
   const uint4* po = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
-  uint4 t[kMaxChunks][4];
-  float mc[kMaxChunks], lc[kMaxChunks];
+  uint4 t[NC][4];
+  float mc[NC], lc[NC];
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NC; ++c) {
     const bool in = c < jb.n_e;
     const size_t sl = slot0 + (size_t)(in ? c : 0) * stride;
     mc[c] = in ? __ldcg(stats + sl * 2 * kTile + r) : -INFINITY;
@@ -656,10 +658,10 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
   }
   float mmax = -INFINITY;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) mmax = fmaxf(mmax, mc[c]);
-  float wc[kMaxChunks], lsum = 0.f;
+  for (int c = 0; c < NC; ++c) mmax = fmaxf(mmax, mc[c]);
+  float wc[NC], lsum = 0.f;
 #pragma unroll
-  for (int c = 0; c < kMaxChunks; ++c) {
+  for (int c = 0; c < NC; ++c) {
     wc[c] = c < jb.n_e ? fast_exp2(mc[c] - mmax) * lc[c] : 0.f;
     lsum += wc[c];
   }
@@ -669,7 +671,7 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
   for (int g = 0; g < 4; ++g) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int c = 0; c < kMaxChunks; ++c) {
+    for (int c = 0; c < NC; ++c) {
       const __half2* h = reinterpret_cast<const __half2*>(&t[c][g]);
 #pragma unroll
       for (int k2 = 0; k2 < 4; ++k2) {
@@ -883,6 +885,7 @@ struct AttnPlan {
   std::vector<uint16_t> cta_off;                  // empty: round-robin over CTAs
   std::vector<uint2> unit_desc;                   // per listed unit, in cta_off order
   std::vector<CombineJob> jobs;                   // split query tiles (one job per tile, all heads)
+  int max_chunks = 1;                             // most chunks of any split tile
 };
 
 // Cost of a unit in key tiles (tensor-core and exp work scale with them), plus a fixed
@@ -969,6 +972,7 @@ AttnPlan plan_attention(int heads, int kv_group, int seq, int d, bool allow_spli
         j.n_e = (uint16_t)nc;
         j.pad = 0;
         p.jobs.push_back(j);
+        p.max_chunks = std::max(p.max_chunks, nc);
       }
       base += nc;
     }
@@ -1039,7 +1043,11 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   ca.ws_o_off = plan.o_off;
   std::copy(plan.jobs.begin(), plan.jobs.end(), ca.job);
   const dim3 grid((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 32)));
-  return launch_pdl(attn_combine_bf16_kernel<D>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
+  if (plan.max_chunks <= 2)
+    return launch_pdl(attn_combine_bf16_kernel<D, 2>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
+  if (plan.max_chunks <= 4)
+    return launch_pdl(attn_combine_bf16_kernel<D, 4>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
+  return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
 }
 
 int check_attn(const char* op, int64_t heads, int64_t seq, int64_t d, int dtype) {
