@@ -611,7 +611,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
 // A query tile whose key range was split over n_e units has n_e partials: (m_c, l_c) per
 // row and O_c / l_c in fp16. The output row is sum_c w_c (O_c / l_c) / sum_c w_c with
 // w_c = 2^(m_c - max m) l_c, summed in chunk order so the result does not depend on the
-// schedule. One CTA of 64 threads covers 64 rows x 32 columns of one (job, head); every
+// schedule. One CTA of 64 threads covers 64 rows x 8 * (8 / NC) columns of one (job,
+// head), so a thread holds 8 partial vectors whatever the chunk count; every
 // partial's loads for a thread are issued together.
 
 constexpr int kMaxCombineJobs = 1024;
@@ -633,18 +634,19 @@ struct CombineArgs {
 // zeros, so every NC gives the same bits).
 template <int D, int NC>
 __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_constant__ CombineArgs args) {
+  constexpr int GPT = 8 / NC;  // 8-column groups per thread: every thread keeps 8 partial loads in flight
   pdl_enter();  // the attention grid before this one has completed and its partials are visible
   const CombineJob jb = args.job[blockIdx.x];
   const int head = blockIdx.y;
   const int r = (blockIdx.z & 1) * 64 + threadIdx.x;  // row within the query tile
-  const int g0 = (blockIdx.z >> 1) * 4;                // first 8-column group of the slice
+  const int g0 = (blockIdx.z >> 1) * GPT;              // first 8-column group of the slice
   const int row = jb.qt * kTile + r;
   if (row >= args.seq) return;
   const size_t stride = (size_t)args.heads;  // unit step between consecutive chunks
   const size_t slot0 = (size_t)jb.v0 * args.heads + head;
   const float* stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
   const uint4* po = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
-  uint4 t[NC][4];
+  uint4 t[NC][GPT];
   float mc[NC], lc[NC];
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
@@ -653,7 +655,7 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     mc[c] = in ? __ldcg(stats + sl * 2 * kTile + r) : -INFINITY;
     lc[c] = in ? __ldcg(stats + sl * 2 * kTile + kTile + r) : 0.f;
 #pragma unroll
-    for (int g = 0; g < 4; ++g)
+    for (int g = 0; g < GPT; ++g)
       t[c][g] = in ? __ldcg(po + sl * (kTile * D / 8) + (size_t)(g0 + g) * kTile + r) : make_uint4(0u, 0u, 0u, 0u);
   }
   float mmax = -INFINITY;
@@ -668,7 +670,7 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
   const float inv = 1.0f / lsum;
   uint4* dst = reinterpret_cast<uint4*>(args.out + ((size_t)head * args.seq + row) * D + g0 * 8);
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
+  for (int g = 0; g < GPT; ++g) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
@@ -1042,12 +1044,13 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   ca.ws_stats_off = plan.stats_off;
   ca.ws_o_off = plan.o_off;
   std::copy(plan.jobs.begin(), plan.jobs.end(), ca.job);
-  const dim3 grid((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 32)));
+  // grid z: (2 row halves) x (8-column groups / groups per thread)
+  auto grid = [&](int nc) { return dim3((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 8) / (8 / nc))); };
   if (plan.max_chunks <= 2)
-    return launch_pdl(attn_combine_bf16_kernel<D, 2>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
+    return launch_pdl(attn_combine_bf16_kernel<D, 2>, grid(2), dim3(64), 0, st, "nkl_attention(combine)", ca);
   if (plan.max_chunks <= 4)
-    return launch_pdl(attn_combine_bf16_kernel<D, 4>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
-  return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid, dim3(64), 0, st, "nkl_attention(combine)", ca);
+    return launch_pdl(attn_combine_bf16_kernel<D, 4>, grid(4), dim3(64), 0, st, "nkl_attention(combine)", ca);
+  return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid(8), dim3(64), 0, st, "nkl_attention(combine)", ca);
 }
 
 int check_attn(const char* op, int64_t heads, int64_t seq, int64_t d, int dtype) {
