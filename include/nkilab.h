@@ -201,6 +201,20 @@ int nkl_attention_gqa(const void* q, const void* k, const void* v, void* out, vo
                       size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq,
                       int64_t head_dim, float scale, int dtype, void* stream);
 
+/* nkl_attention_gqa on strided q [heads, seq, head_dim], k and v [kv_heads, seq,
+ * head_dim] and out [heads, seq, head_dim]: each is addressed as element (h, s, e) at
+ * h * head_stride + s * seq_stride + e (strides in elements, positive multiples of 8,
+ * i.e. 16 bytes; k and v share theirs), so q/k/v can be read straight out of a fused
+ * [seq, 3, heads, head_dim] projection and out written as [seq, heads, head_dim] with no
+ * transposing copies. bf16 only (NKL_ERR_DTYPE otherwise); workspace as
+ * nkl_attention_ws. No reference counterpart: the reference transposes on the host
+ * (nkilab/model.py:83-88). */
+int nkl_attention_strided(const void* q, const void* k, const void* v, void* out, void* workspace,
+                          size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq,
+                          int64_t head_dim, int64_t q_seq_stride, int64_t q_head_stride,
+                          int64_t kv_seq_stride, int64_t kv_head_stride, int64_t out_seq_stride,
+                          int64_t out_head_stride, float scale, int dtype, void* stream);
+
 /* Bytes of device workspace nkl_attention_naive needs: fp32 scores and dtype
  * probabilities, each [heads, seq, seq]. */
 size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype);

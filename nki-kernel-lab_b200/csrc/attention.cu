@@ -627,6 +627,7 @@ struct CombineArgs {
   bf16* out;
   int heads, seq, n_jobs;
   size_t ws_stats_off, ws_o_off;
+  int64_t o_ss, o_hs;  // output strides in elements: between rows (seq) and between heads
   CombineJob job[kMaxCombineJobs];
 };
 
@@ -668,7 +669,7 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     lsum += wc[c];
   }
   const float inv = 1.0f / lsum;
-  uint4* dst = reinterpret_cast<uint4*>(args.out + ((size_t)head * args.seq + row) * D + g0 * 8);
+  uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)head * args.o_hs + (size_t)row * args.o_ss + g0 * 8);
 #pragma unroll
   for (int g = 0; g < GPT; ++g) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -871,14 +872,26 @@ naive_softmax_kernel(const float* __restrict__ scores, TP* __restrict__ probs, i
 
 // ------------------------------------------------------------------ host
 
-int make_qkv_map(CUtensorMap* m, const void* base, int heads, int seq, int d, const char* what) {
+// [heads, seq, d] bf16 with the given seq and head strides (elements; d is contiguous).
+int make_qkv_map(CUtensorMap* m, const void* base, int heads, int seq, int d, int64_t seq_stride,
+                 int64_t head_stride, const char* what) {
   const uint64_t dims[3] = {(uint64_t)d, (uint64_t)seq, (uint64_t)heads};
-  const uint64_t strides[2] = {(uint64_t)d * 2, (uint64_t)seq * d * 2};
+  const uint64_t strides[2] = {(uint64_t)seq_stride * 2, (uint64_t)head_stride * 2};
   const uint32_t box[3] = {64, (uint32_t)kTile, 1};
   return make_tensor_map_bf16(m, base, 3, dims, strides, box, what);
 }
 
 inline size_t round256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Element strides of q, k, v and out: between consecutive rows of a head (seq) and
+// between heads; the head dimension is contiguous. Contiguous [heads, seq, d] tensors
+// have seq stride d and head stride seq * d.
+struct AttnLayout {
+  int64_t q_ss, q_hs, k_ss, k_hs, v_ss, v_hs, o_ss, o_hs;
+};
+inline AttnLayout contiguous_layout(int64_t seq, int64_t d) {
+  return AttnLayout{d, seq * d, d, seq * d, d, seq * d, d, seq * d};
+}
 
 // Work decomposition and CTA schedule, shared by the workspace-size query and the launch.
 struct AttnPlan {
@@ -996,12 +1009,12 @@ const AttnPlan& cached_plan(int heads, int kv_group, int seq, int d, bool allow_
 
 template <int D>
 int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int heads, int kv_heads, int seq,
-                     float scale, void* ws, size_t ws_bytes, cudaStream_t st) {
+                     float scale, void* ws, size_t ws_bytes, const AttnLayout& lay, cudaStream_t st) {
   CUtensorMap mq, mk, mv, mo;
-  int rc = make_qkv_map(&mq, q, heads, seq, D, "nkl_attention(q)");
-  if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, "nkl_attention(k)");
-  if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, "nkl_attention(v)");
-  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, "nkl_attention(out)");
+  int rc = make_qkv_map(&mq, q, heads, seq, D, lay.q_ss, lay.q_hs, "nkl_attention(q)");
+  if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, lay.k_ss, lay.k_hs, "nkl_attention(k)");
+  if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, lay.v_ss, lay.v_hs, "nkl_attention(v)");
+  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)");
   if (rc) return rc;
   const AttnPlan& plan = cached_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
@@ -1043,6 +1056,8 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   ca.n_jobs = (int)plan.jobs.size();
   ca.ws_stats_off = plan.stats_off;
   ca.ws_o_off = plan.o_off;
+  ca.o_ss = lay.o_ss;
+  ca.o_hs = lay.o_hs;
   std::copy(plan.jobs.begin(), plan.jobs.end(), ca.job);
   // grid z: (2 row halves) x (8-column groups / groups per thread)
   auto grid = [&](int nc) { return dim3((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 8) / (8 / nc))); };
@@ -1082,7 +1097,7 @@ namespace {
 // one unit.
 int attention_impl(const char* op, const void* q, const void* k, const void* v, void* out, void* workspace,
                    size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq, int64_t head_dim,
-                   float scale, int dtype, void* stream) {
+                   float scale, int dtype, void* stream, const AttnLayout* layout = nullptr) {
   int rc = check_attn(op, heads, seq, head_dim, dtype);
   if (rc) return rc;
   if (heads == 0 || seq == 0) return NKL_OK;
@@ -1091,6 +1106,9 @@ int attention_impl(const char* op, const void* q, const void* k, const void* v, 
                 (long long)kv_heads);
   if (!q || !k || !v || !out) return fail(NKL_ERR_ARG, "%s: NULL pointer", op);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (layout && dtype != NKL_BFLOAT16)
+    return fail(NKL_ERR_DTYPE, "%s: strided q/k/v/out are supported for bf16 only", op);
+  const AttnLayout lay = layout ? *layout : contiguous_layout(seq, head_dim);
   if (dtype == NKL_FLOAT32) {
     dim3 grid((unsigned)((seq + kF32Rows - 1) / kF32Rows), (unsigned)heads);
     attn_fwd_f32_kernel<<<grid, 128, 0, st>>>(static_cast<const float*>(q), static_cast<const float*>(k),
@@ -1106,9 +1124,9 @@ int attention_impl(const char* op, const void* q, const void* k, const void* v, 
   if (workspace && !is_aligned(workspace, 256)) return fail(NKL_ERR_ALIGN, "%s: workspace not 256-byte aligned", op);
   if (head_dim == 64)
     return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                                workspace ? workspace_bytes : 0, st);
+                                workspace ? workspace_bytes : 0, lay, st);
   return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                               workspace ? workspace_bytes : 0, st);
+                               workspace ? workspace_bytes : 0, lay, st);
 }
 
 }  // namespace
@@ -1136,6 +1154,25 @@ extern "C" int nkl_attention_gqa(const void* q, const void* k, const void* v, vo
                                  int64_t head_dim, float scale, int dtype, void* stream) {
   return attention_impl("nkl_attention_gqa", q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr,
                         workspace_bytes, heads, kv_heads, seq, head_dim, scale, dtype, stream);
+}
+
+extern "C" int nkl_attention_strided(const void* q, const void* k, const void* v, void* out, void* workspace,
+                                     size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq,
+                                     int64_t head_dim, int64_t q_seq_stride, int64_t q_head_stride,
+                                     int64_t kv_seq_stride, int64_t kv_head_stride, int64_t out_seq_stride,
+                                     int64_t out_head_stride, float scale, int dtype, void* stream) {
+  const char* op = "nkl_attention_strided";
+  const int64_t st[6] = {q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride, out_seq_stride, out_head_stride};
+  for (int i = 0; i < 6; ++i)
+    if (st[i] < 1 || st[i] % 8 != 0 || st[i] > (int64_t(1) << 38))
+      return fail(NKL_ERR_ALIGN, "%s: strides must be positive multiples of 8 elements (16 bytes), got %lld", op,
+                  (long long)st[i]);
+  if (q_seq_stride < head_dim || kv_seq_stride < head_dim || out_seq_stride < head_dim)
+    return fail(NKL_ERR_SHAPE, "%s: a row stride is smaller than head_dim", op);
+  const AttnLayout lay{q_seq_stride, q_head_stride, kv_seq_stride, kv_head_stride,
+                       kv_seq_stride, kv_head_stride, out_seq_stride, out_head_stride};
+  return attention_impl(op, q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr, workspace_bytes, heads,
+                        kv_heads, seq, head_dim, scale, dtype, stream, &lay);
 }
 
 extern "C" size_t nkl_attention_naive_workspace_size(int64_t heads, int64_t seq, int dtype) {

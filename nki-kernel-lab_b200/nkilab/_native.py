@@ -51,6 +51,8 @@ SIGNATURES = {
     "nkl_attention": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "nkl_attention_ws": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
+    "nkl_attention_strided": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
+                                     _i64, _f, _int, _p]),
     "nkl_attention_gqa": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_naive_workspace_size": (_sz, [_i64, _i64, _int]),
     "nkl_attention_naive": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),

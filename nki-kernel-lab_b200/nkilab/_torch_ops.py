@@ -244,3 +244,36 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, n
 @attention.register_fake
 def _(q, k, v, scale, naive):
     return torch.empty_like(q)
+
+
+@torch.library.custom_op("nkilab::attention_strided_", mutates_args=("out",))
+def attention_strided_(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, scale: float) -> None:
+    """Causal attention into `out` for strided views: q and out [H, S, d], k and v
+    [Hkv, S, d], each with unit stride along d and any head / seq strides that are
+    multiples of 8 elements (k and v with equal strides), e.g. q = qkv[:, 0].transpose(0, 1)
+    of a [S, 3, H, d] projection and out = o.view(S, H, d).transpose(0, 1). bf16 only."""
+    dev = q.device
+    for t in (k, v, out):
+        if t.device != dev or t.dtype != q.dtype:
+            raise RuntimeError("attention_strided_: tensors must share device and dtype")
+    if dev.type != "cuda" or q.dtype != torch.bfloat16:
+        raise RuntimeError("attention_strided_: bf16 CUDA tensors only")
+    H, S, d = q.shape
+    Hkv = k.shape[0]
+    if (k.shape != v.shape or k.shape[1:] != q.shape[1:] or out.shape != q.shape or Hkv < 1 or H % Hkv
+            or k.stride() != v.stride() or any(t.stride(2) != 1 for t in (q, k, v, out))):
+        raise ValueError(f"q {tuple(q.shape)}/{q.stride()}, k {tuple(k.shape)}/{k.stride()}, "
+                         f"v {tuple(v.shape)}/{v.stride()}, out {tuple(out.shape)}/{out.stride()}: bad layout")
+    dt = dtype_code(q)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    with torch.cuda.device(dev):
+        nbytes = N.lib.nkl_attention_workspace_size(H, S, d, dt)
+        ws = _attention_workspace(dev, st, nbytes) if nbytes else None
+        N.call("nkl_attention_strided", q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+               ws.data_ptr() if ws is not None else None, nbytes, H, Hkv, S, d, q.stride(1), q.stride(0),
+               k.stride(1), k.stride(0), out.stride(1), out.stride(0), scale, dt, st)
+
+
+@attention_strided_.register_fake
+def _(q, k, v, out, scale):
+    return None

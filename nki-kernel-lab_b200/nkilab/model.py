@@ -18,6 +18,7 @@ attention over all B*H heads. Rotary embeddings are left out, as in the referenc
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass
 
 import numpy as np
@@ -115,9 +116,18 @@ def _forward_device(block: DecoderBlock, x: torch.Tensor, attention_variant: str
     x2 = x.reshape(-1, d)
     h = ops.rmsnorm(x2, w["norm1"], cfg.eps)
     qkv = ops.matmul(h, w["wqkv"]).view(B, S, 3, H, hd)
-    q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).reshape(B * H, S, hd) for i in range(3))
-    a = ops.attention(q, k, v, variant=attention_variant)
-    a = a.view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B * S, d)
+    if attention_variant != "naive" and x.dtype == torch.bfloat16 and hd in (64, 128):
+        # q, k, v read straight out of the fused projection and the output written in the
+        # [B*S, d] layout the Wo GEMM reads: strided views, no transposing copies
+        a = torch.empty(B, S, H, hd, dtype=x.dtype, device=x.device)
+        for b in range(B):
+            q, k, v = (qkv[b, :, i].transpose(0, 1) for i in range(3))
+            torch.ops.nkilab.attention_strided_(q, k, v, a[b].transpose(0, 1), 1.0 / math.sqrt(hd))
+        a = a.view(B * S, d)
+    else:
+        q, k, v = (qkv[:, :, i].permute(0, 2, 1, 3).reshape(B * H, S, hd) for i in range(3))
+        a = ops.attention(q, k, v, variant=attention_variant)
+        a = a.view(B, H, S, hd).permute(0, 2, 1, 3).reshape(B * S, d)
     # residual add fused with the second RMSNorm (same rounding as add-then-norm)
     x2, h = torch.ops.nkilab.add_rmsnorm(x2.contiguous(), ops.matmul(a, w["wo"]).contiguous(), w["norm2"], cfg.eps)
     if "wgu" in w:

@@ -1,6 +1,8 @@
 """GPU parity of causal attention (tcgen05 flash bf16, exact fp32 flash, naive)."""
 from __future__ import annotations
 
+import math
+
 import ml_dtypes
 import numpy as np
 import pytest
@@ -240,3 +242,21 @@ def test_split_kv_workspace_under_cuda_graph_replay():
         assert torch.equal(o_graph, o_eager), f"replay {trial}"
     _check_vs_oracle(o_graph, q.cpu(), k.cpu(), v.cpu())
 
+
+
+@pytest.mark.parametrize("H,Hkv,S,D", [(8, 8, 2048, 128), (32, 32, 1000, 128), (8, 2, 700, 64)])
+def test_strided_attention_matches_contiguous_bit_for_bit(ops, H, Hkv, S, D):
+    """nkl_attention_strided reading q/k/v straight out of a fused [S, q|k|v, heads, d]
+    projection and writing out as [S, H, d]: the same kernels on the same plan as the
+    contiguous entry point, so the same bits (split-KV combine included at 8x2048)."""
+    g = torch.Generator(device="cuda").manual_seed(H + S)
+    width = (H + 2 * Hkv) * D
+    qkv = torch.randn(S, width, device="cuda", generator=g).to(torch.bfloat16)
+    q = qkv[:, :H * D].view(S, H, D).transpose(0, 1)
+    k = qkv[:, H * D:(H + Hkv) * D].view(S, Hkv, D).transpose(0, 1)
+    v = qkv[:, (H + Hkv) * D:].view(S, Hkv, D).transpose(0, 1)
+    o = torch.full((S, H, D), float("nan"), dtype=torch.bfloat16, device="cuda")
+    torch.ops.nkilab.attention_strided_(q, k, v, o.transpose(0, 1), 1.0 / math.sqrt(D))
+    ref = ops.attention(q.contiguous(), k.contiguous(), v.contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(o.transpose(0, 1), ref)

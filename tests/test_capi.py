@@ -98,3 +98,18 @@ def test_workspace_sizes_and_checks(native):
 def test_errors_raise_with_message(native):
     with pytest.raises(native.NklError, match="nkl_matmul.*multiples of 8"):
         native.call("nkl_matmul", FAKE, FAKE, FAKE, 16, 16, 7, native.BFLOAT16, None)
+
+
+def test_attention_strided_rejects_bad_strides_before_device_work(native):
+    """Strides must be positive multiples of 8 elements and rows at least head_dim long;
+    checked before any CUDA call."""
+    L = native.lib
+    ok = dict(qs=384, qh=128, ks=384, kh=128, os_=256, oh=128)
+    def call(**kw):
+        a = {**ok, **kw}
+        return L.nkl_attention_strided(FAKE, FAKE, FAKE, FAKE, None, 0, 2, 2, 128, 128, a["qs"], a["qh"], a["ks"],
+                                       a["kh"], a["os_"], a["oh"], 0.1, native.BFLOAT16, None)
+    assert call(qs=388) == native.ERR_ALIGN
+    assert call(kh=0) == native.ERR_ALIGN
+    assert call(oh=-128) == native.ERR_ALIGN
+    assert call(os_=64) == native.ERR_SHAPE
