@@ -162,6 +162,12 @@ def shard_block(block, world: int, rank: int, dtype: torch.dtype, device) -> Sha
             heads=(h0, h1), ff=(f0, f1))
 
 
+
+def _device_ops():
+    from . import ops
+
+    return ops
+
 def decoder_block(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights] = None,
                   variant: str = "flash_pipelined", group=None, ops_module=None) -> torch.Tensor:
     """Tensor-parallel DecoderBlock forward. x: [S, d] full input on every rank.
@@ -180,10 +186,18 @@ def decoder_block(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights]
     h = all_gather_dim0(ops_module.rmsnorm(x_loc.contiguous(), w.norm1, cfg.eps), S, group)
     if nh > 0:
         qkv = ops_module.matmul(h, w.wqkv)
-        q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].reshape(S, nh, hd).transpose(0, 1).contiguous()
-                   for i in range(3))
-        a = ops_module.attention(q, k, v, variant=variant)
-        part = ops_module.matmul(a.transpose(0, 1).reshape(S, nh * hd).contiguous(), w.wo)
+        if (ops_module is _device_ops() and qkv.is_cuda and qkv.dtype == torch.bfloat16 and variant != "naive"
+                and hd in (64, 128)):
+            # local heads read straight out of the projection, output in the Wo layout
+            a = torch.empty(S, nh, hd, dtype=qkv.dtype, device=qkv.device)
+            q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].view(S, nh, hd).transpose(0, 1) for i in range(3))
+            torch.ops.nkilab.attention_strided_(q, k, v, a.transpose(0, 1), 1.0 / math.sqrt(hd))
+            part = ops_module.matmul(a.view(S, nh * hd), w.wo)
+        else:
+            q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].reshape(S, nh, hd).transpose(0, 1).contiguous()
+                       for i in range(3))
+            a = ops_module.attention(q, k, v, variant=variant)
+            part = ops_module.matmul(a.transpose(0, 1).reshape(S, nh * hd).contiguous(), w.wo)
     else:
         part = torch.zeros((S, d), dtype=x.dtype, device=x.device)
     x_loc = (x_loc.float() + reduce_scatter_dim0(part, group).float()).to(x.dtype)
