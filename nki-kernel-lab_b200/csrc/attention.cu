@@ -315,7 +315,23 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   // Launched with programmatic dependent launch: the prologue above (barriers, TMEM,
   // descriptor prefetch) overlaps the previous kernel of the stream; nothing in global
   // memory (q, k, v, the output, the workspace a previous combine kernel may still be
-  // reading) is touched before that kernel has completed and its writes are visible.
+  // reading) is read or written before that kernel has completed and its writes are
+  // visible. Before waiting, the producer asks L2 to prefetch the first unit's Q, K and
+  // V tiles: a prefetch only warms L2, the point of coherence, so a tile the previous
+  // kernel is still writing is read correctly by the loads after the wait; it just lets
+  // those first loads hit L2 instead of HBM.
+  if (warp == kProducerWarp && elect_one()) {
+    UnitRun u0;
+    if (next_unit(args, 0, u0)) {
+      for (int c = 0; c < kSub; ++c) {
+        tma_prefetch_3d(&map_q, c * 64, u0.qt * kTile, u0.head);
+        tma_prefetch_3d(&map_k, c * 64, u0.j0 * kTile, u0.kv_head);
+        tma_prefetch_3d(&map_v, c * 64, u0.j0 * kTile, u0.kv_head);
+        if (u0.n > 1) tma_prefetch_3d(&map_k, c * 64, (u0.j0 + 1) * kTile, u0.kv_head);
+      }
+    }
+  }
+  __syncwarp();
   asm volatile("griddepcontrol.wait;" ::: "memory");
 
   if (warp == kProducerWarp) {
