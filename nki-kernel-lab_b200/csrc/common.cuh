@@ -123,6 +123,21 @@ __device__ __forceinline__ void pdl_enter() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// The two halves of pdl_enter, for kernels that prefetch between them.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// Ask L2 to fetch [p, p + bytes) (p 16-byte aligned, bytes a multiple of 16). Issued
+// before pdl_wait it overlaps a kernel's first HBM reads with the previous kernel's
+// tail; a prefetch only warms L2, the point of coherence, so it is correct even while
+// the previous kernel is still writing that memory (the loads after the wait read the
+// final data).
+__device__ __forceinline__ void l2_prefetch(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
 template <typename... KArgs, typename... Args>
 int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, const char* what,
                Args... args) {

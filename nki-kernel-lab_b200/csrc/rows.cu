@@ -67,9 +67,11 @@ __global__ void __launch_bounds__(kRmsWarpsPerBlock * 32, rms_min_blocks(NV))
 rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restrict__ y, int64_t rows, int cols,
                     float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
-  pdl_enter();
+  pdl_launch_dependents();
   const int64_t row = (int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (row < rows && lane == 0) l2_prefetch(x + row * cols, (uint32_t)(cols * sizeof(T)));
+  pdl_wait();
   if (row >= rows) return;
   const int nvec = cols / V;
   const T* xr = x + row * cols;
@@ -164,9 +166,11 @@ template <typename T, int NV, bool FULL>
 __global__ void __launch_bounds__(kSoftmaxWarpsPerBlock * 32)
 softmax_warp_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t rows, int cols) {
   constexpr int V = Vec16<T>::N;
-  pdl_enter();
+  pdl_launch_dependents();
   const int64_t row = (int64_t)blockIdx.x * kSoftmaxWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (row < rows && lane == 0) l2_prefetch(x + row * cols, (uint32_t)(cols * sizeof(T)));
+  pdl_wait();
   if (row >= rows) return;
   const int nvec = cols / V;
   const T* xr = x + row * cols;
@@ -297,7 +301,14 @@ template <typename T>
 __global__ void __launch_bounds__(kSwigluThreads)
 swiglu_vec_kernel(const T* __restrict__ g, const T* __restrict__ u, T* __restrict__ y, int64_t nvec) {
   constexpr int V = Vec16<T>::N;
-  pdl_enter();
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {  // this block's contiguous span of gate and up
+    const int64_t v0 = (int64_t)blockIdx.x * kSwigluThreads * kSwigluUnroll;
+    const int64_t nv = nvec - v0 < (int64_t)kSwigluThreads * kSwigluUnroll ? nvec - v0 : (int64_t)kSwigluThreads * kSwigluUnroll;
+    l2_prefetch(g + v0 * V, (uint32_t)(nv * 16));
+    l2_prefetch(u + v0 * V, (uint32_t)(nv * 16));
+  }
+  pdl_wait();
   const int64_t base = (int64_t)blockIdx.x * kSwigluThreads * kSwigluUnroll + threadIdx.x;
   Vec16<T> gv[kSwigluUnroll], uv[kSwigluUnroll];
 #pragma unroll
@@ -337,9 +348,14 @@ __global__ void __launch_bounds__(kAddRmsWarpsPerBlock * 32)
 add_rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
                         T* __restrict__ s_out, T* __restrict__ y, int64_t rows, int cols, float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
-  pdl_enter();
+  pdl_launch_dependents();
   const int64_t row = (int64_t)blockIdx.x * kAddRmsWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  if (row < rows && lane == 0 && (cols * sizeof(T)) % 16 == 0) {
+    l2_prefetch(x + row * cols, (uint32_t)(cols * sizeof(T)));
+    l2_prefetch(res + row * cols, (uint32_t)(cols * sizeof(T)));
+  }
+  pdl_wait();
   if (row >= rows) return;
   const int nvec = cols / V;
   Vec16<T> sv[NV];
