@@ -73,6 +73,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                     bf16* __restrict__ c, int M, int N, int K, int m_tiles, int n_tiles) {
   extern __shared__ uint8_t smem_raw[];
+  pdl_launch_dependents();
   auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                       ~uintptr_t(1023));
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -106,6 +107,23 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s.tmem_base;
+  // Launched with programmatic dependent launch: the prologue above overlaps the previous
+  // kernel of the stream, and A, B and C are touched only after its writes are visible.
+  // Before waiting, the producer asks L2 for the first tile's first k-blocks (a prefetch
+  // only warms L2, the point of coherence: an operand the previous kernel is still
+  // writing is read correctly by the loads after the wait).
+  if (warp == 0 && elect_one() && (int)blockIdx.x < num_tiles) {
+    int mt, nt;
+    tile_coords(blockIdx.x, m_tiles, n_tiles, mt, nt);
+    const int pre = k_blocks < STAGES ? k_blocks : STAGES;
+    for (int kb = 0; kb < pre; ++kb) {
+      tma_prefetch_2d(&map_a, kb * kBK, mt * kBM);
+#pragma unroll
+      for (int j = 0; j < BN / 64; ++j) tma_prefetch_2d(&map_b, nt * BN + j * 64, kb * kBK);
+    }
+  }
+  __syncwarp();
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------- TMA producer
@@ -349,9 +367,8 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
     if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_matmul: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
-  gemm_bf16_tc_kernel<BN, STAGES, EPI><<<grid, kGemmThreads, smem, st>>>(ma, mb, static_cast<bf16*>(c), M, N, K,
-                                                                          m_tiles, n_tiles);
-  return check_launch("nkl_matmul");
+  return launch_pdl(gemm_bf16_tc_kernel<BN, STAGES, EPI>, dim3(grid), dim3(kGemmThreads), smem, st, "nkl_matmul", ma,
+                    mb, static_cast<bf16*>(c), M, N, K, m_tiles, n_tiles);
 }
 
 int check_gemm(const char* op, int64_t M, int64_t N, int64_t K, int dtype) {
