@@ -133,6 +133,15 @@ int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int64_t N, int6
 int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N, int64_t K,
                      int dtype, void* stream);
 
+/* GEMM with the residual add in its epilogue: out[M, N] = residual[M, N] + a[M, K] . b[K, N],
+ * bf16 only, with a . b rounded to bf16 before the add and the sum rounded once more, as
+ * nkl_matmul followed by a bf16 add rounds it (so both paths give the same bits). out may
+ * be residual itself. K, N multiples of 8, 16-byte-aligned pointers.
+ * Replaces nkilab/model.py:89 (x + matmul(act, Wd)): the residual add after the down
+ * projection, folded into the GEMM so the block makes no separate pass over it. */
+int nkl_matmul_residual(const void* a, const void* b, const void* residual, void* out, int64_t M,
+                        int64_t N, int64_t K, int dtype, void* stream);
+
 /* Fused gate/up projection with SwiGLU: out[M, F] = silu(a . Wg) * (a . Wu), bf16 only.
  * b_gate_up is [K, 2F] row-major with the columns of Wg and Wu interleaved in blocks of
  * 128 (columns 256*i .. 256*i+127 = Wg[:, 128*i ..], the next 128 = Wu[:, 128*i ..]).

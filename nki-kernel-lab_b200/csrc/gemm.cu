@@ -65,13 +65,16 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 
 // EPI: kEpiStore writes C = A.B in bf16. kEpiSwiglu takes B as [gate | up] column blocks
 // of 128 (see nkl_matmul_swiglu) and writes silu(gate) * up, each rounded to bf16 first
-// exactly as the unfused matmul -> swiglu path rounds them, into C[M, N/2].
-constexpr int kEpiStore = 0, kEpiSwiglu = 1;
+// exactly as the unfused matmul -> swiglu path rounds them, into C[M, N/2]. kEpiResidual
+// writes C = R + A.B with A.B rounded to bf16 first and the sum rounded once more, as a
+// bf16 matmul followed by a bf16 add rounds it.
+constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2;
 
 template <int BN, int STAGES, int EPI = kEpiStore>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    bf16* __restrict__ c, int M, int N, int K, int m_tiles, int n_tiles) {
+                    bf16* __restrict__ c, const bf16* __restrict__ res, int M, int N, int K, int m_tiles,
+                    int n_tiles) {
   extern __shared__ uint8_t smem_raw[];
   pdl_launch_dependents();
   auto& s = *reinterpret_cast<GemmSmem<BN, STAGES>*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -242,6 +245,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         continue;
       }
       bf16* crow = c + (int64_t)gm * N;
+      const bf16* rrow = EPI == kEpiResidual ? res + (int64_t)gm * N : nullptr;
 #pragma unroll 1
       for (int cc = 0; cc < BN / 32; ++cc) {
         uint32_t r[32];
@@ -255,6 +259,12 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
               float f[8];
 #pragma unroll
               for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
+              if constexpr (EPI == kEpiResidual) {
+                Vec16<bf16> rv;
+                rv.raw = *reinterpret_cast<const uint4*>(rrow + gn + v * 8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(__float2bfloat16_rn(f[e])) + rv.get(e);
+              }
               *reinterpret_cast<uint4*>(crow + gn + v * 8) = pack16<bf16>(f);
             }
           }
@@ -336,7 +346,8 @@ gemm_naive_kernel(const T* __restrict__ A, const T* __restrict__ B, T* __restric
 // ------------------------------------------------------------------ host
 
 template <int BN, int STAGES, int EPI = kEpiStore>
-int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaStream_t st) {
+int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaStream_t st,
+              const void* res = nullptr) {
   CUtensorMap ma, mb;
   {
     const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
@@ -368,7 +379,23 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
     if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   return launch_pdl(gemm_bf16_tc_kernel<BN, STAGES, EPI>, dim3(grid), dim3(kGemmThreads), smem, st, "nkl_matmul", ma,
-                    mb, static_cast<bf16*>(c), M, N, K, m_tiles, n_tiles);
+                    mb, static_cast<bf16*>(c), static_cast<const bf16*>(res), M, N, K, m_tiles, n_tiles);
+}
+
+// Tile width by how many tiles the SMs get. 256-column tiles read 96 B/clk of MMA
+// operands from shared memory per SM and keep the tensor pipe fed; 128-column tiles need
+// 128 B/clk, at the limit, so they are used only when 256-column tiles would leave more
+// than half of the SMs idle, and 64-column tiles (more CTAs, smaller operands) when
+// 128-column tiles would.
+template <int EPI>
+int dispatch_tc(const void* a, const void* b, void* c, const void* res, int64_t M, int64_t N, int64_t K,
+                cudaStream_t st) {
+  const int64_t m_tiles = (M + kBM - 1) / kBM;
+  const int64_t tiles256 = m_tiles * ((N + 255) / 256);
+  const int64_t tiles128 = m_tiles * ((N + 127) / 128);
+  if (2 * tiles256 >= sm_count()) return launch_tc<256, 4, EPI>(a, b, c, (int)M, (int)N, (int)K, st, res);
+  if (2 * tiles128 <= sm_count()) return launch_tc<64, 8, EPI>(a, b, c, (int)M, (int)N, (int)K, st, res);
+  return launch_tc<128, 6, EPI>(a, b, c, (int)M, (int)N, (int)K, st, res);
 }
 
 int check_gemm(const char* op, int64_t M, int64_t N, int64_t K, int dtype) {
@@ -413,17 +440,22 @@ extern "C" int nkl_matmul(const void* a, const void* b, void* c, int64_t M, int6
                 (long long)N);
   if (!is_aligned(a, 16) || !is_aligned(b, 16) || !is_aligned(c, 16))
     return fail(NKL_ERR_ALIGN, "nkl_matmul: bf16 operands must be 16-byte aligned");
-  // Tile width by how many tiles the SMs get. 256-column tiles read 96 B/clk of MMA
-  // operands from shared memory per SM and keep the tensor pipe fed; 128-column tiles
-  // need 128 B/clk, at the limit, so they are used only when 256-column tiles would
-  // leave more than half of the SMs idle, and 64-column tiles (more CTAs, smaller
-  // operands) when 128-column tiles would.
-  const int64_t m_tiles = (M + kBM - 1) / kBM;
-  const int64_t tiles256 = m_tiles * ((N + 255) / 256);
-  const int64_t tiles128 = m_tiles * ((N + 127) / 128);
-  if (2 * tiles256 >= sm_count()) return launch_tc<256, 4>(a, b, c, (int)M, (int)N, (int)K, st);
-  if (2 * tiles128 <= sm_count()) return launch_tc<64, 8>(a, b, c, (int)M, (int)N, (int)K, st);
-  return launch_tc<128, 6>(a, b, c, (int)M, (int)N, (int)K, st);
+  return dispatch_tc<kEpiStore>(a, b, c, nullptr, M, N, K, st);
+}
+
+extern "C" int nkl_matmul_residual(const void* a, const void* b, const void* residual, void* out, int64_t M,
+                                   int64_t N, int64_t K, int dtype, void* stream) {
+  int rc = check_gemm("nkl_matmul_residual", M, N, K, dtype);
+  if (rc) return rc;
+  if (dtype != NKL_BFLOAT16) return fail(NKL_ERR_DTYPE, "nkl_matmul_residual: bf16 only");
+  if (M == 0 || N == 0) return NKL_OK;
+  if (!a || !b || !residual || !out) return fail(NKL_ERR_ARG, "nkl_matmul_residual: NULL pointer");
+  if (K == 0 || K % 8 != 0 || N % 8 != 0)
+    return fail(NKL_ERR_SHAPE, "nkl_matmul_residual: needs K > 0 and K, N multiples of 8 (got K=%lld N=%lld)",
+                (long long)K, (long long)N);
+  if (!is_aligned(a, 16) || !is_aligned(b, 16) || !is_aligned(residual, 16) || !is_aligned(out, 16))
+    return fail(NKL_ERR_ALIGN, "nkl_matmul_residual: operands must be 16-byte aligned");
+  return dispatch_tc<kEpiResidual>(a, b, out, residual, M, N, K, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int nkl_matmul_swiglu(const void* a, const void* b_gate_up, void* out, int64_t M, int64_t F, int64_t K,

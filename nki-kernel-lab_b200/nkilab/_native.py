@@ -48,6 +48,7 @@ SIGNATURES = {
     "nkl_matmul": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_naive": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_swiglu": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "nkl_matmul_residual": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_attention": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "nkl_attention_ws": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),

@@ -192,6 +192,26 @@ def _(a, b_gate_up):
     return a.new_empty((a.shape[0], b_gate_up.shape[1] // 2))
 
 
+@torch.library.custom_op("nkilab::matmul_residual", mutates_args=())
+def matmul_residual(a: torch.Tensor, b: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """residual + a @ b with the add in the GEMM epilogue (bf16; same bits as matmul, then add)."""
+    dev, dt, st = _prep(a, b, residual)
+    M, K = a.shape
+    K2, Ncols = b.shape
+    if K != K2 or residual.shape != (M, Ncols):
+        raise ValueError(f"a {tuple(a.shape)}, b {tuple(b.shape)}, residual {tuple(residual.shape)}: shapes do not match")
+    out = torch.empty((M, Ncols), dtype=a.dtype, device=dev)
+    with torch.cuda.device(dev):
+        N.call("nkl_matmul_residual", a.data_ptr(), b.data_ptr(), residual.data_ptr(), out.data_ptr(), M, Ncols, K,
+               dt, st)
+    return out
+
+
+@matmul_residual.register_fake
+def _(a, b, residual):
+    return a.new_empty((a.shape[0], b.shape[1]))
+
+
 # Split-KV workspaces of the bf16 attention kernel, one per (device, stream), grown on
 # demand (the kernels need no initialised contents). Calls on one stream are ordered, so
 # they can share it; other streams get their own.

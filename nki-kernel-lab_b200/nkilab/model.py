@@ -134,7 +134,10 @@ def _forward_device(block: DecoderBlock, x: torch.Tensor, attention_variant: str
         act = torch.ops.nkilab.matmul_swiglu(h.contiguous(), w["wgu"])
     else:
         act = ops.swiglu(ops.matmul(h, w["wg"]), ops.matmul(h, w["wu"]))
-    out = x2 + ops.matmul(act, w["wd"])
+    if x.dtype == torch.bfloat16:  # residual add in the down projection's epilogue (same bits)
+        out = torch.ops.nkilab.matmul_residual(act.contiguous(), w["wd"], x2.contiguous())
+    else:
+        out = x2 + ops.matmul(act, w["wd"])
     return out.view(*lead, d)
 
 

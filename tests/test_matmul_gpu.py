@@ -156,3 +156,19 @@ def test_matmul_swiglu_rejects_bad_shapes(ops):
     assert rc == N.ERR_SHAPE and "F % 128" in N.lib.nkl_last_error().decode()
     rc = N.lib.nkl_matmul_swiglu(a.data_ptr(), b.data_ptr(), out.data_ptr(), 128, 128, 64, N.FLOAT32, st)
     assert rc == N.ERR_DTYPE
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 384), (4096, 4096, 11008), (1000, 264, 72), (3, 8, 8)])
+def test_matmul_residual_equals_matmul_then_add(M, N, K):
+    """The residual add folded into the GEMM epilogue gives the same bits as a bf16 matmul
+    followed by a bf16 add (the product is rounded to bf16 before the add)."""
+    from nkilab import ops
+
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    a = (torch.rand(M, K, device="cuda", generator=g) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand(K, N, device="cuda", generator=g) * 2 - 1).to(torch.bfloat16)
+    r = torch.randn(M, N, device="cuda", generator=g).to(torch.bfloat16)
+    got = torch.ops.nkilab.matmul_residual(a, b, r)
+    ref = r + ops.matmul(a, b)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
