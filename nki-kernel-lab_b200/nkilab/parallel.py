@@ -123,6 +123,39 @@ def row_op(op: str, *tensors: torch.Tensor, group=None, compute: Optional[Callab
     return all_gather_dim0(local, R, group)
 
 
+def matmul(a: torch.Tensor, b: torch.Tensor, group=None, compute: Optional[Callable] = None,
+           block: int = 128) -> torch.Tensor:
+    """Column-sharded GEMM: c = a @ b with b's columns split over the ranks in units of
+    `block` columns (so every local bf16 GEMM keeps N a multiple of 8); each rank multiplies
+    the full a by its column block of b, then one all-gather assembles the full [M, N]
+    c on every rank. a: [M, K], b: [K, N], the same full tensors on every rank."""
+    world, rank = _world(group)
+    N = b.shape[1]
+    units = (N + block - 1) // block
+    u0, u1 = shard_range(units, world, rank)
+    c0, c1 = min(u0 * block, N), min(u1 * block, N)
+    if compute is None:
+        from . import ops
+
+        compute = ops.matmul
+    if c1 > c0:
+        local = compute(a, b[:, c0:c1].contiguous())
+    else:
+        local = torch.zeros((a.shape[0], 0), dtype=a.dtype, device=a.device)
+    if world == 1:
+        return local
+    # gather the column blocks as row blocks of c^T (all_gather_dim0 shards dim 0)
+    sizes = [shard_range(units, world, r) for r in range(world)]
+    widths = [min(e * block, N) - min(s * block, N) for s, e in sizes]
+    max_w = max(widths)
+    lt = local.t().contiguous()
+    if lt.shape[0] != max_w:
+        lt = torch.cat([lt, torch.zeros((max_w - lt.shape[0], lt.shape[1]), dtype=lt.dtype, device=lt.device)], 0)
+    out = torch.empty((world * max_w, lt.shape[1]), dtype=lt.dtype, device=lt.device)
+    dist.all_gather_into_tensor(out, lt, group=group)
+    return torch.cat([out[r * max_w:r * max_w + widths[r]] for r in range(world)], 0).t().contiguous()
+
+
 # --------------------------------------------------------------------------- decoder block
 
 @dataclass

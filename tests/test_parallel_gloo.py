@@ -75,6 +75,12 @@ def _worker_collectives(rank, world, port):
         ops = _oracle_ops()
         out = P.attention(q, k, v, compute=lambda a, b, c, var: ops.attention(a, b, c, var))
         assert torch.equal(out, O.attention_flash(q, k, v))
+        # GEMM, columns of b sharded in 128-column units (300 columns: uneven, last unit partial)
+        a = torch.randn(17, 40, generator=g)
+        b = torch.randn(40, 300, generator=g)
+        c = P.matmul(a, b, compute=O.matmul)
+        assert c.shape == (17, 300)
+        assert torch.equal(c, O.matmul(a, b))
     finally:
         dist.destroy_process_group()
 

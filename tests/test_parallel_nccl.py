@@ -1,9 +1,9 @@
 """nkilab.parallel on real GPUs: world_size-2 NCCL process groups, one process per GPU.
 
-Head-sharded attention and row-sharded RMSNorm are checked against the same ops run
-on one GPU (the shards go through the same kernels, so rows match exactly and
-attention matches to the split-plan rounding), and the tensor-parallel decoder block
-against the single-GPU block. Runs only where at least two GPUs are visible; the
+Head-sharded attention, row-sharded RMSNorm and the column-sharded GEMM are checked
+against the same ops run on one GPU (the shards go through the same kernels, so rows and
+GEMM columns match exactly and attention matches to the split-plan rounding), and the
+tensor-parallel decoder block against the single-GPU block. Runs only where at least two GPUs are visible; the
 processes are started with `spawn`."""
 from __future__ import annotations
 
@@ -52,6 +52,12 @@ def _worker(rank: int, world: int, port: int) -> None:
         x = torch.randn(4096, 2048, generator=g).to(torch.bfloat16).to(dev)
         w = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
         assert torch.equal(P.row_op("rmsnorm", x, w, eps=1e-6), ops.rmsnorm(x, w, 1e-6))
+
+        # column-sharded GEMM (128-column units of b per rank, all-gather of c): the same
+        # k-ordered accumulation per output column as the one-GPU GEMM, so the same bits
+        a = (torch.rand(256, 512, generator=g) * 2 - 1).to(torch.bfloat16).to(dev)
+        b = (torch.rand(512, 1000, generator=g) * 2 - 1).to(torch.bfloat16).to(dev)
+        assert torch.equal(P.matmul(a, b), ops.matmul(a, b))
 
         # tensor-parallel decoder block (heads and FFN columns sharded, reduce-scatter after Wo / Wd)
         torch.manual_seed(3)
