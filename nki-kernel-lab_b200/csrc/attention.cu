@@ -141,7 +141,6 @@ struct AttnSmem {
   uint64_t pv_step;    // one phase per P.V tile
   uint64_t pv_done;    // one phase per unit: its last P.V complete
   uint64_t o_free;     // engine has read O (all engine threads)
-  uint64_t eng_sync;   // output staging complete (all engine threads)
   uint64_t mma_done;
   float xmax[2][2 * kTile];  // [tile parity][half * 128 + row]: row-max exchange
   float xsum[2 * kTile];     // [half * 128 + row]: row-sum exchange
@@ -159,6 +158,7 @@ struct AttnArgs {
   unsigned char* ws;  // NULL when no query tile is split
   int heads, q_tiles, chunk, units;
   int kv_group;  // query heads per key/value head (1 = multi-head, heads = multi-query)
+  int seq;
   float scale_log2;
   size_t ws_stats_off, ws_o_off;  // byte offsets of the partial (max, sum) and O regions
   int n_ctas_listed;              // > 0: cta_off / unit_desc give each CTA's units
@@ -285,7 +285,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s.q_full[i], 1);
-      mbar_init(&s.q_empty[i], 1);
+      mbar_init(&s.q_empty[i], 4);  // one arrival per TMEM lane quadrant
       mbar_init(&s.k_full[i], 1);
       mbar_init(&s.k_empty[i], 1);
       mbar_init(&s.v_full[i], 1);
@@ -296,7 +296,6 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     mbar_init(&s.pv_step, 1);
     mbar_init(&s.pv_done, 1);
     mbar_init(&s.o_free, kEngineThreads);
-    mbar_init(&s.eng_sync, kEngineThreads);
     mbar_init(&s.mma_done, 1);
     s.abort = 0;
     fence_barrier_init();
@@ -485,8 +484,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     const uint32_t o_addr = tmem + lane_off + kOCol0 + (uint32_t)(hf * (D / 2));
     const int pair_id = 1 + qd;
     const int sw = r & 7;
-    const bool lead = threadIdx.x == 0;  // issues the output stores and frees the Q buffer
-    uint32_t gt = 0, uc = 0, xc = 0;
+    const bool quad_lead = hf == 0 && lane == 0;  // stores its quadrant's output rows, frees the Q buffer
+    uint32_t gt = 0, uc = 0;
     bool ok = true;
     UnitRun un;
     for (int i = 0; ok && next_unit(args, i, un); ++i) {
@@ -597,19 +596,21 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
           uint8_t* rowp = s.q[qb] + (g / 8) * (kTile * 128) + r * 128;
           *reinterpret_cast<uint4*>(rowp + (((g & 7) ^ sw) * 16)) = pack16<bf16>(f);
         }
+        // Each lane quadrant stores its own 32 rows as soon as its two warps have staged
+        // them (no CTA-wide barrier); rows past seq are clipped by the TMA unit.
         fence_proxy_async_smem();
-        mbar_arrive(&s.eng_sync);
-        if (!warp_wait(&s.eng_sync, xc & 1u, &s.abort, 38)) { ok = false; break; }
-        ++xc;
-        if (lead) {  // rows past seq are clipped by the TMA unit
+        pair_sync(pair_id);
+        const int row0 = qt * kTile + qd * 32;
+        if (quad_lead && row0 < args.seq) {
 #pragma unroll
-          for (int c = 0; c < kSub; ++c) tma_store_3d(&map_o, s.q[qb] + c * (kTile * 128), c * 64, qt * kTile, un.head);
+          for (int c = 0; c < kSub; ++c)
+            tma_store_3d(&map_o, s.q[qb] + c * (kTile * 128) + qd * 32 * 128, c * 64, row0, un.head);
           tma_store_commit();
           tma_store_wait_read();
         }
       }
-      // the Q buffer may be refilled once the output staging has been read
-      if (lead) mbar_arrive(&s.q_empty[qb]);
+      // the Q buffer may be refilled once every quadrant's output staging has been read
+      if (quad_lead) mbar_arrive(&s.q_empty[qb]);
       gt += (uint32_t)un.n;
       ++uc;
     }
@@ -888,12 +889,13 @@ naive_softmax_kernel(const float* __restrict__ scores, TP* __restrict__ probs, i
 
 // ------------------------------------------------------------------ host
 
-// [heads, seq, d] bf16 with the given seq and head strides (elements; d is contiguous).
+// [heads, seq, d] bf16 with the given seq and head strides (elements; d is contiguous),
+// moved in boxes of 64 columns x box_rows rows.
 int make_qkv_map(CUtensorMap* m, const void* base, int heads, int seq, int d, int64_t seq_stride,
-                 int64_t head_stride, const char* what) {
+                 int64_t head_stride, const char* what, int box_rows = kTile) {
   const uint64_t dims[3] = {(uint64_t)d, (uint64_t)seq, (uint64_t)heads};
   const uint64_t strides[2] = {(uint64_t)seq_stride * 2, (uint64_t)head_stride * 2};
-  const uint32_t box[3] = {64, (uint32_t)kTile, 1};
+  const uint32_t box[3] = {64, (uint32_t)box_rows, 1};
   return make_tensor_map_bf16(m, base, 3, dims, strides, box, what);
 }
 
@@ -1030,7 +1032,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   int rc = make_qkv_map(&mq, q, heads, seq, D, lay.q_ss, lay.q_hs, "nkl_attention(q)");
   if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, lay.k_ss, lay.k_hs, "nkl_attention(k)");
   if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, lay.v_ss, lay.v_hs, "nkl_attention(v)");
-  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)");
+  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)", 32);
   if (rc) return rc;
   const AttnPlan& plan = cached_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
@@ -1048,6 +1050,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;
   a.heads = heads;
   a.kv_group = heads / kv_heads;
+  a.seq = seq;
   a.q_tiles = plan.q_tiles;
   a.chunk = plan.chunk;
   a.units = plan.units;
