@@ -435,13 +435,15 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         for (int t = 0; ok && t < n; ++t) {
           const uint32_t G = gt + (uint32_t)t;
           const int b = G & 1;
-          if (!mbar_wait(&s.p_full[b], (G >> 1) & 1u, &s.abort, &g_attn_dev_error, 22)) { ok = false; break; }
+          // V(t) and the free O (first tile of a unit) are normally ready long before P(t):
+          // take those waits first, so only the P.V issue itself follows P(t).
+          const uint32_t vi = vc + (uint32_t)t;
+          if (!mbar_wait(&s.v_full[vi & 1], (vi >> 1) & 1u, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
           if (t == 0 && !mbar_wait(&s.o_free, (uc & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 23)) {
             ok = false;
             break;
           }
-          const uint32_t vi = vc + (uint32_t)t;
-          if (!mbar_wait(&s.v_full[vi & 1], (vi >> 1) & 1u, &s.abort, &g_attn_dev_error, 24)) { ok = false; break; }
+          if (!mbar_wait(&s.p_full[b], (G >> 1) & 1u, &s.abort, &g_attn_dev_error, 22)) { ok = false; break; }
           tc_fence_after();
           const uint64_t vd = (vi & 1) ? v_desc1 : v_desc0;
 #pragma unroll
