@@ -214,14 +214,19 @@ def _(a, b, residual):
 
 # Split-KV workspaces of the bf16 attention kernel, one per (device, stream), grown on
 # demand (the kernels need no initialised contents). Calls on one stream are ordered, so
-# they can share it; other streams get their own.
+# they can share it; other streams get their own. A workspace outgrown by a larger shape
+# is kept alive rather than freed: a CUDA graph captured earlier still holds its address
+# and writes to it on every replay, so its memory must not go back to the allocator.
 _attention_ws: dict = {}
+_retired_ws: list = []
 
 
 def _attention_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
     key = (dev.index, stream)
     ws = _attention_ws.get(key)
     if ws is None or ws.numel() < nbytes:
+        if ws is not None:
+            _retired_ws.append(ws)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         _attention_ws[key] = ws
     return ws

@@ -94,3 +94,20 @@ def test_block_weights_follow_reference_seeding():
     assert names == ["norm1.weight", "norm2.weight", "wqkv.weight", "wo.weight", "wg.weight", "wu.weight", "wd.weight"]
     w1 = b.norm1.weight.detach()
     assert float(w1.min()) >= 0.5 and float(w1.max()) <= 1.5
+
+
+def test_grown_attention_workspace_stays_alive():
+    """A CUDA graph captured with the smaller workspace keeps writing to it on replay, so
+    growing the per-stream workspace must not release the old one."""
+    import torch
+
+    from nkilab import _torch_ops as T
+
+    dev, stream = torch.device("cpu"), -12345  # a key no real stream uses
+    small = T._attention_workspace(dev, stream, 256)
+    assert T._attention_workspace(dev, stream, 128) is small  # big enough: reused
+    big = T._attention_workspace(dev, stream, 1024)
+    assert big is not small and big.numel() >= 1024
+    assert any(w is small for w in T._retired_ws)
+    T._attention_ws.pop((dev.index, stream))
+    T._retired_ws[:] = [w for w in T._retired_ws if w is not small]
