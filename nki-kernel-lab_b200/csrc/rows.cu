@@ -636,6 +636,10 @@ extern "C" int nkl_softmax(const void* x, void* out, int64_t rows, int64_t cols,
 
 extern "C" size_t nkl_softmax_unfused_workspace_size(int64_t rows, int64_t cols) {
   if (rows <= 0 || cols <= 0) return 0;
+  // rows * cols fp32 values plus two fp32 per row; sizes whose byte count does not fit
+  // in size_t report SIZE_MAX, which no workspace can satisfy
+  const size_t limit = (SIZE_MAX - 4096) / sizeof(float);
+  if ((uint64_t)cols > limit || (uint64_t)rows > limit / (uint64_t)cols) return SIZE_MAX;
   return 2 * round256((size_t)rows * sizeof(float)) + round256((size_t)rows * (size_t)cols * sizeof(float));
 }
 
@@ -645,6 +649,9 @@ extern "C" int nkl_softmax_unfused(const void* x, void* out, void* workspace, si
   if (rc) return rc;
   if (rows == 0) return NKL_OK;
   if (!x || !out || !workspace) return fail(NKL_ERR_ARG, "nkl_softmax_unfused: NULL pointer");
+  if (nkl_softmax_unfused_workspace_size(rows, cols) == SIZE_MAX)
+    return fail(NKL_ERR_SHAPE, "nkl_softmax_unfused: [%lld, %lld] is too large for any workspace", (long long)rows,
+                (long long)cols);
   if (workspace_bytes < nkl_softmax_unfused_workspace_size(rows, cols))
     return fail(NKL_ERR_ARG, "nkl_softmax_unfused: workspace %zu B < required %zu B", workspace_bytes,
                 nkl_softmax_unfused_workspace_size(rows, cols));
@@ -713,8 +720,11 @@ extern "C" int nkl_softmax_unfused_static(const void* x, void* out, int64_t rows
   if (rc) return rc;
   if (rows == 0) return NKL_OK;
   if (!x || !out) return fail(NKL_ERR_ARG, "nkl_softmax_unfused_static: NULL pointer");
-  const size_t need = nkl_softmax_unfused_workspace_size(rows, cols);
-  if (need > (size_t)NKL_SOFTMAX_UNFUSED_STATIC_BYTES)
+  // rows * cols is bounded before any product is formed, so no size can wrap around
+  constexpr uint64_t kStaticFloats = NKL_SOFTMAX_UNFUSED_STATIC_BYTES / sizeof(float);
+  const bool fits = (uint64_t)cols <= kStaticFloats && (uint64_t)rows <= kStaticFloats / (uint64_t)cols;
+  const size_t need = fits ? nkl_softmax_unfused_workspace_size(rows, cols) : SIZE_MAX;
+  if (!fits || need > (size_t)NKL_SOFTMAX_UNFUSED_STATIC_BYTES)
     return fail(NKL_ERR_SHAPE,
                 "nkl_softmax_unfused_static: [%lld, %lld] needs %zu B of scratch, above the fixed %zu B "
                 "(use nkl_softmax_unfused with a caller-owned workspace)",

@@ -212,21 +212,23 @@ def _(a, b, residual):
     return a.new_empty((a.shape[0], b.shape[1]))
 
 
-# Split-KV workspaces of the bf16 attention kernel, one per (device, stream), grown on
-# demand (the kernels need no initialised contents). Calls on one stream are ordered, so
-# they can share it; other streams get their own. A workspace outgrown by a larger shape
-# is kept alive rather than freed: a CUDA graph captured earlier still holds its address
-# and writes to it on every replay, so its memory must not go back to the allocator.
+# Split-KV workspaces of the bf16 attention kernel. Eager calls share one workspace per
+# (device, stream), grown on demand (the kernels need no initialised contents): calls on
+# one stream are ordered, so they can share it, and other streams get their own. A call
+# made while its stream is being captured into a CUDA graph takes a fresh workspace from
+# the caching allocator instead, which during capture hands out memory of the graph's
+# own pool: every graph then owns the workspaces it writes, two graphs can be replayed
+# concurrently, and replacing an outgrown eager workspace never frees memory a graph
+# still uses.
 _attention_ws: dict = {}
-_retired_ws: list = []
 
 
 def _attention_workspace(dev: torch.device, stream: int, nbytes: int) -> torch.Tensor:
+    if dev.type == "cuda" and torch.cuda.is_current_stream_capturing():
+        return torch.empty(nbytes, dtype=torch.uint8, device=dev)
     key = (dev.index, stream)
     ws = _attention_ws.get(key)
     if ws is None or ws.numel() < nbytes:
-        if ws is not None:
-            _retired_ws.append(ws)
         ws = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         _attention_ws[key] = ws
     return ws

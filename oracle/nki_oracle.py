@@ -32,8 +32,8 @@ def _f32(x: torch.Tensor) -> torch.Tensor:
 # --------------------------------------------------------------------------- row kernels
 
 def softmax_fused(x: torch.Tensor) -> torch.Tensor:
-    """nkilab/kernels/norm.py:65-89: neg_max = -max (:161), e = exp(x + neg_max) with
-    the row sum in the same step (:164-165), rinv = 1/sum (:167), y = e * rinv (:169)."""
+    """nkilab/kernels/norm.py:65-89: neg_max = -max (:79), e = exp(x + neg_max) with
+    the row sum in the same step (:82-83), rinv = 1/sum (:85), y = e * rinv (:87)."""
     xf = _f32(x)
     neg_max = -xf.amax(dim=-1, keepdim=True)
     e = torch.exp(xf + neg_max)
@@ -43,8 +43,8 @@ def softmax_fused(x: torch.Tensor) -> torch.Tensor:
 
 
 def softmax_unfused(x: torch.Tensor) -> torch.Tensor:
-    """nkilab/kernels/norm.py:22-62: m = max (:121), e = exp(x - m) (:129-131),
-    s = sum e (:133), y = e / s (:142)."""
+    """nkilab/kernels/norm.py:22-62: m = max (:39), e = exp(x - m) (:47-49),
+    s = sum e (:51), y = e / s (:60)."""
     xf = _f32(x)
     m = xf.amax(dim=-1, keepdim=True)
     e = torch.exp(xf - m)
@@ -52,33 +52,34 @@ def softmax_unfused(x: torch.Tensor) -> torch.Tensor:
     return (e / s).to(x.dtype)
 
 
-def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
-    """nkilab/kernels/norm.py:92-118: ssq = sum(x^2) fp32 (:189-190),
-    ms = ssq * (1/D) + eps (:192), rstd = rsqrt(ms) (:194), xn = x * rstd fp32 (:196),
-    y = xn * weight rounded to x.dtype (:198)."""
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6, acc: torch.dtype = torch.float32) -> torch.Tensor:
+    """nkilab/kernels/norm.py:92-118: ssq = sum(x^2) fp32 (:107-108),
+    ms = ssq * (1/D) + eps (:110), rstd = rsqrt(ms) (:112), xn = x * rstd fp32 (:114),
+    y = xn * weight rounded to x.dtype (:116). `acc` (float32 as the reference, or
+    float64 for an error floor) is the precision of every intermediate."""
     D = x.shape[-1]
-    xf = _f32(x)
+    xf = x.to(acc)
     ssq = (xf * xf).sum(dim=-1, keepdim=True)
-    ms = ssq * torch.tensor(1.0 / D, dtype=torch.float32) + torch.tensor(eps, dtype=torch.float32)
+    ms = ssq * torch.tensor(1.0 / D, dtype=acc) + torch.tensor(eps, dtype=acc)
     rstd = torch.rsqrt(ms)
     xn = xf * rstd
-    return (xn * _f32(weight.to(x.dtype))).to(x.dtype)
+    return (xn * weight.to(x.dtype).to(acc)).to(x.dtype)
 
 
-def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
-    """nkilab/kernels/norm.py:121-136: a = silu(gate) fp32 (:213-214), y = a * up
-    rounded to gate.dtype (:215-216)."""
-    g = _f32(gate)
+def swiglu(gate: torch.Tensor, up: torch.Tensor, acc: torch.dtype = torch.float32) -> torch.Tensor:
+    """nkilab/kernels/norm.py:121-136: a = silu(gate) fp32 (:131-132), y = a * up
+    rounded to gate.dtype (:133-134)."""
+    g = gate.to(acc)
     a = g / (1.0 + torch.exp(-g))
-    return (a * _f32(up)).to(gate.dtype)
+    return (a * up.to(acc)).to(gate.dtype)
 
 
 # --------------------------------------------------------------------------- matmul
 
-def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+def matmul(a: torch.Tensor, b: torch.Tensor, acc: torch.dtype = torch.float32) -> torch.Tensor:
     """nkilab/kernels/matmul.py:46-82 (and :24-43): fp32 accumulation of exact products
-    (PSUM), one rounding to lhsT.dtype = a.dtype on the copy out (:76-79)."""
-    return (_f32(a) @ _f32(b)).to(a.dtype)
+    (PSUM, :62-75), one rounding to lhsT.dtype = a.dtype on the copy out (:76-79)."""
+    return (a.to(acc) @ b.to(acc)).to(a.dtype)
 
 
 def choose_blocks(m_tiles: int, n_tiles: int) -> tuple[int, int]:
@@ -105,7 +106,8 @@ def _pad_seq(t: torch.Tensor, Sp: int) -> torch.Tensor:
     return out
 
 
-def attention_flash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None) -> torch.Tensor:
+def attention_flash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
+                    acc: torch.dtype = torch.float32) -> torch.Tensor:
     """Causal flash attention as nkilab/kernels/attention.py:280-325 with the balanced
     update :204-246 (the default "flash_pipelined" variant), batched over heads.
 
@@ -119,6 +121,8 @@ def attention_flash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
         corr = exp(-nm + nm') (:232-233); l = l * corr + rsum (:234-236)
         o = o * corr + p @ v_j (fp32 accumulate) (:237-245)
       out_i = o * (1/l) rounded to v.dtype (:137-142)
+    `acc` is the precision of scores, statistics and accumulators (float32 as the
+    reference; float64 gives an error floor with the same bf16 rounding points).
     """
     H, S, d = q.shape
     if scale is None:
@@ -126,21 +130,21 @@ def attention_flash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
     dt = v.dtype
     nt = -(-S // T)
     Sp = nt * T
-    qf, kf, vf = (_f32(_pad_seq(t, Sp)) for t in (q, k, v))
+    qf, kf, vf = (_pad_seq(t, Sp).to(acc) for t in (q, k, v))
     out = torch.empty((H, Sp, d), dtype=dt)
-    sc = torch.tensor(scale, dtype=torch.float32)
+    sc = torch.tensor(scale, dtype=acc)
     rows = torch.arange(T).view(T, 1)
     cols = torch.arange(T).view(1, T)
     diag_keep = (rows - cols) >= 0
     for i in range(nt):
         qi = qf[:, i * T:(i + 1) * T]
-        nm = torch.full((H, T, 1), -NEG_INF, dtype=torch.float32)
-        l = torch.zeros((H, T, 1), dtype=torch.float32)
-        o = torch.zeros((H, T, d), dtype=torch.float32)
+        nm = torch.full((H, T, 1), -NEG_INF, dtype=acc)
+        l = torch.zeros((H, T, 1), dtype=acc)
+        o = torch.zeros((H, T, d), dtype=acc)
         for j in range(i + 1):
             s = qi @ kf[:, j * T:(j + 1) * T].transpose(1, 2)
             if j == i:
-                s = torch.where(diag_keep, s, torch.tensor(NEG_INF, dtype=torch.float32))
+                s = torch.where(diag_keep, s, torch.tensor(NEG_INF, dtype=acc))
             tmax = s.amax(dim=-1, keepdim=True)
             nm_new = torch.minimum(tmax * (-sc), nm)
             e = torch.exp(s * sc + nm_new)
@@ -148,7 +152,7 @@ def attention_flash(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
             p = e.to(dt)
             corr = torch.exp(nm * -1.0 + nm_new)
             l = l * corr + rsum
-            pv = _f32(p) @ vf[:, j * T:(j + 1) * T]
+            pv = p.to(acc) @ vf[:, j * T:(j + 1) * T]
             o = o * corr + pv
             nm = nm_new
         linv = 1.0 / l
@@ -183,10 +187,13 @@ def attention_naive(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: fl
 
 def decoder_block(x: torch.Tensor, norm1: torch.Tensor, wqkv: torch.Tensor, wo: torch.Tensor, norm2: torch.Tensor,
                   wg: torch.Tensor, wu: torch.Tensor, wd: torch.Tensor, n_heads: int, eps: float = 1e-6,
-                  naive_attention: bool = False) -> torch.Tensor:
+                  naive_attention: bool = False, acc: torch.dtype = torch.float32) -> torch.Tensor:
     """nkilab/model.py:70-89 (nki_forward) for x [S, d]: weights are given in
     nn.Linear layout [out, in] and used transposed in x's dtype (:76-77); residual adds
-    in x.dtype (:86, :89)."""
+    in x.dtype (:86, :89). `acc` as in attention_flash: float64 keeps every bf16
+    rounding point of the block and removes the fp32 accumulation error, so the
+    distance between the float32 and float64 results is the floor two correct fp32
+    implementations of the block can be expected to differ by."""
     S, d = x.shape
     hd = d // n_heads
     dt = x.dtype
@@ -194,11 +201,11 @@ def decoder_block(x: torch.Tensor, norm1: torch.Tensor, wqkv: torch.Tensor, wo: 
     def w(m: torch.Tensor) -> torch.Tensor:
         return m.t().contiguous().to(dt)
 
-    h = rmsnorm(x, norm1.to(dt), eps)
-    qkv = matmul(h, w(wqkv))
+    h = rmsnorm(x, norm1.to(dt), eps, acc)
+    qkv = matmul(h, w(wqkv), acc)
     q, k, v = (qkv[:, i * d:(i + 1) * d].reshape(S, n_heads, hd).transpose(0, 1).contiguous() for i in range(3))
-    a = (attention_naive if naive_attention else attention_flash)(q, k, v)
-    x = (_f32(x) + _f32(matmul(a.transpose(0, 1).reshape(S, d), w(wo)))).to(dt)
-    h = rmsnorm(x, norm2.to(dt), eps)
-    act = swiglu(matmul(h, w(wg)), matmul(h, w(wu)))
-    return (_f32(x) + _f32(matmul(act, w(wd)))).to(dt)
+    a = attention_naive(q, k, v) if naive_attention else attention_flash(q, k, v, acc=acc)
+    x = (x.to(acc) + matmul(a.transpose(0, 1).reshape(S, d), w(wo), acc).to(acc)).to(dt)
+    h = rmsnorm(x, norm2.to(dt), eps, acc)
+    act = swiglu(matmul(h, w(wg), acc), matmul(h, w(wu), acc), acc)
+    return (x.to(acc) + matmul(act, w(wd), acc).to(acc)).to(dt)

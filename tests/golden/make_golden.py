@@ -1,6 +1,8 @@
 """Generate the golden vectors in this directory from the reference's own code.
 
-    python tests/golden/make_golden.py [--reference PATH]   (default PATH: /root/reference)
+    python tests/golden/make_golden.py --reference PATH   (or NKL_REFERENCE=PATH in the environment)
+
+PATH is a checkout of Nags-gk/nki-kernel-lab.
 
 Runs the unmodified Nags-gk/nki-kernel-lab sources -- nkilab/ops.py host wrappers,
 nkilab/kernels/*.py NKI kernels and nkilab/model.py -- with nki_shim.py standing in
@@ -40,8 +42,11 @@ def put(store: dict, key: str, arr) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("NKL_REFERENCE"),
+                    help="checkout of Nags-gk/nki-kernel-lab (default: $NKL_REFERENCE)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference PATH or set NKL_REFERENCE")
 
     sys.path.insert(0, HERE)
     import nki_shim

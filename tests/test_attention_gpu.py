@@ -244,6 +244,40 @@ def test_split_kv_workspace_under_cuda_graph_replay():
 
 
 
+def test_graphs_captured_with_default_settings_replay_concurrently():
+    """Two CUDA graphs of the split-KV attention op, captured with torch.cuda.graph's
+    defaults (one shared capture stream), replayed at the same time on two streams: each
+    graph owns the workspace it captured, so the replays do not race and each matches an
+    eager call on its own inputs bit for bit."""
+    H, S, D = 8, 2048, 128
+    g = torch.Generator(device="cuda").manual_seed(17)
+    ins = [[torch.randn(H, S, D, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3)] for _ in range(2)]
+    scale = 1.0 / math.sqrt(D)
+    for t in ins:  # plan and kernel attributes set up before capture
+        torch.ops.nkilab.attention(*t, scale, False)
+    torch.cuda.synchronize()
+    graphs, outs = [], []
+    for t in ins:
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            outs.append(torch.ops.nkilab.attention(*t, scale, False))
+        graphs.append(gr)
+    ref = [torch.ops.nkilab.attention(*t, scale, False) for t in ins]
+    torch.cuda.synchronize()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    for _ in range(5):
+        for o in outs:
+            o.fill_(float("nan"))
+        torch.cuda.synchronize()
+        for gr, st in zip(graphs, streams):
+            with torch.cuda.stream(st):
+                for _ in range(4):
+                    gr.replay()
+        torch.cuda.synchronize()
+        for o, r in zip(outs, ref):
+            assert torch.equal(o, r)
+
+
 @pytest.mark.parametrize("H,Hkv,S,D", [(8, 8, 2048, 128), (32, 32, 1000, 128), (8, 2, 700, 64)])
 def test_strided_attention_matches_contiguous_bit_for_bit(ops, H, Hkv, S, D):
     """nkl_attention_strided reading q/k/v straight out of a fused [S, q|k|v, heads, d]

@@ -21,6 +21,7 @@ import pytest
 import torch
 
 from conftest import rel_err
+from oracle import nki_oracle as O
 
 pytestmark = pytest.mark.gpu
 
@@ -54,9 +55,13 @@ def test_static_scratch_matches_workspace_entry_point(dtype, rows, cols):
         rc = N.lib.nkl_softmax_unfused(_p(x), _p(y_ws), _p(ws), nbytes, rows, cols, code[dtype], st)
         assert rc == N.OK, N.lib.nkl_last_error()
         torch.cuda.synchronize()
-        a, b = y_static.float().cpu().numpy(), y_ws.float().cpu().numpy()
+        # the same three kernels on the same input: the same bits, and the oracle's
+        # restatement of the reference's unfused softmax within the usual tolerance
+        assert torch.equal(y_static, y_ws)
+        a = y_static.float().cpu().numpy()
         assert np.isfinite(a).all()
-        assert rel_err(a, b) < (1e-5 if dtype == torch.float32 else 1e-2)
+        ref = O.softmax_unfused(x.cpu()).float().numpy()
+        assert rel_err(a, ref) < (1e-5 if dtype == torch.float32 else 1e-2)
     N.check_device(stream)
 
 
@@ -72,3 +77,19 @@ def test_static_scratch_rejects_inputs_that_do_not_fit():
     assert b"scratch" in N.lib.nkl_last_error()
     torch.cuda.synchronize()
     assert torch.count_nonzero(y) == 0  # nothing was launched
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 1 << 62), (3, 1 << 61), (1 << 30, 1 << 33)])
+def test_static_scratch_rejects_sizes_whose_byte_count_overflows(rows, cols):
+    """rows * cols * 4 wraps around 64 bits for these shapes; the size check is done
+    before any product is formed, so they are refused rather than launched. The
+    pointers are never touched: the call returns before any launch."""
+    N, code = _codes()
+    y = torch.zeros(16, device="cuda")
+    rc = N.lib.nkl_softmax_unfused_static(_p(y), _p(y), rows, cols, code[torch.float32],
+                                          ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    assert rc == N.ERR_SHAPE
+    assert b"scratch" in N.lib.nkl_last_error()
+    assert N.lib.nkl_softmax_unfused_workspace_size(rows, cols) == ctypes.c_size_t(-1).value
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(y) == 0
