@@ -142,6 +142,16 @@ int nkl_matmul_naive(const void* a, const void* b, void* c, int64_t M, int64_t N
 int nkl_matmul_residual(const void* a, const void* b, const void* residual, void* out, int64_t M,
                         int64_t N, int64_t K, int dtype, void* stream);
 
+/* c[M,N] = a[M,K] @ b[K,N] with bf16 a and b and the fp32 accumulator written unrounded
+ * into a float c (dtype must be NKL_BFLOAT16: it names the inputs). For tensor-parallel
+ * layers whose per-GPU partial products are summed across GPUs before the one rounding
+ * the single-GPU product gets, so the sharded result rounds where the unsharded one does.
+ * K, N multiples of 8, 16-byte-aligned pointers.
+ * Replaces nkilab/kernels/matmul.py:62-79 (the fp32 PSUM accumulators before their cast on
+ * copy-out) for the sharded Wo and Wd products of nkilab/model.py:86,89. */
+int nkl_matmul_f32out(const void* a, const void* b, float* c, int64_t M, int64_t N, int64_t K, int dtype,
+                      void* stream);
+
 /* Fused gate/up projection with SwiGLU: out[M, F] = silu(a . Wg) * (a . Wu), bf16 only.
  * b_gate_up is [K, 2F] row-major with the columns of Wg and Wu interleaved in blocks of
  * 128 (columns 256*i .. 256*i+127 = Wg[:, 128*i ..], the next 128 = Wu[:, 128*i ..]).
@@ -223,6 +233,32 @@ int nkl_attention_strided(const void* q, const void* k, const void* v, void* out
                           int64_t head_dim, int64_t q_seq_stride, int64_t q_head_stride,
                           int64_t kv_seq_stride, int64_t kv_head_stride, int64_t out_seq_stride,
                           int64_t out_head_stride, float scale, int dtype, void* stream);
+
+/* Launch modes of the bf16 flash kernels, the B200 rungs of the reference's flash ladder
+ * (nkilab/kernels/attention.py:155-325, README.md:17-23):
+ *   NKL_ATTN_AUTO             what nkl_attention_ws runs: one 128-row query tile per CTA
+ *                             with S double buffered in TMEM, causal key ranges split over
+ *                             all SMs where that balances the work (flash_balanced's goal)
+ *   NKL_ATTN_ONE_TILE_UNSPLIT the same kernel with every query tile in one unit, no
+ *                             workspace (flash / flash_kv_resident: K and V reused from L2)
+ *   NKL_ATTN_TWO_TILE         two query tiles per CTA interleaved on the tensor core and two
+ *                             softmax warp groups (flash_pipelined's ILP = 2 interleave);
+ *                             head_dim 128, seq a multiple of 256
+ * Every mode computes the same softmax with the reference's rounding points. */
+#define NKL_ATTN_AUTO 0
+#define NKL_ATTN_ONE_TILE_UNSPLIT 1
+#define NKL_ATTN_TWO_TILE 2
+
+/* Workspace bytes nkl_attention_mode uses for this shape and mode (0: none needed). */
+size_t nkl_attention_mode_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype, int mode);
+
+/* nkl_attention_ws with an explicit launch mode (above); the same layouts, workspace rules
+ * and errors, plus NKL_ERR_SHAPE when NKL_ATTN_TWO_TILE does not fit the shape.
+ * Replaces nkilab/ops.py:77-91 (attention, variant=...) -> nkilab/kernels/attention.py:155-325,
+ * one launch mode per rung of the reference's flash ladder. */
+int nkl_attention_mode(const void* q, const void* k, const void* v, void* out, void* workspace,
+                       size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim, float scale, int dtype,
+                       int mode, void* stream);
 
 /* Bytes of device workspace nkl_attention_naive needs: fp32 scores and dtype
  * probabilities, each [heads, seq, seq]. */

@@ -10,9 +10,10 @@
 // dtype=vdtype), key tiles after the diagonal skipped (:166), final O * (1/l) rounded
 // once (:137-142). The running max is kept in the log2 domain (scale * log2(e) folded
 // into one FMA before a hardware exp2); mathematically the same exp(scale*s - m).
-// The reference rescales O on every key tile; here O is rescaled only when a row's
-// running max grows by more than 2^8 (P values stay <= 256, exact in fp32 and
-// relatively exact in bf16), which gives the same softmax up to rounding.
+// As in the reference (attention.py:224-245), P is taken relative to the running max
+// m updated on every key tile, and O and l are multiplied by exp(m_old - m_new) whenever
+// m grows (the reference multiplies on every tile; where m is unchanged the factor is 1),
+// so P is rounded to bf16 at the reference's scale.
 //
 // bf16 kernel (sm_100a): persistent, one CTA per SM.
 //   work unit  (head, query tile, chunk of its causal key range); the host orders units
@@ -22,7 +23,7 @@
 //              the partials in chunk order, so the result does not depend on the schedule
 //   warps 0-7  softmax engine: two warps per TMEM lane quadrant, each taking 64 of the
 //              128 keys of every score row (row maxima and sums exchanged through shared
-//              memory). Per key tile: tcgen05.ld of the scores, row max, lazy rescale of
+//              memory). Per key tile: tcgen05.ld of the scores, row max, rescale of
 //              O in TMEM, exp2 with the scale folded into one FMA, P (bf16 pairs)
 //              written back over the score columns with tcgen05.st
 //   warp 8     TMA producer: Q per unit (double buffered), K and V through 2-deep rings
@@ -60,7 +61,6 @@ constexpr int kProducerWarp = kEngineWarps;
 constexpr int kMmaWarp = kEngineWarps + 1;
 constexpr int kAttnThreads = kEngineThreads + 64;
 constexpr float kLog2e = 1.4426950408889634f;
-constexpr float kRescaleLog2 = 8.0f;  // rescale O only when the row max grows by > 2^8
 constexpr int kMaxCtas = 192;         // schedule table capacity (>= SMs of any sm_100 part)
 constexpr int kMaxSched = 1024;       // units listed explicitly; more units: round-robin
 constexpr int kMaxChunks = 8;         // a query tile's key range is split into at most 8 units
@@ -517,33 +517,35 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         xm[hf * kTile + r] = max64(v);
         pair_sync(pair_id);
         const float mx = fmaxf(xm[r], xm[kTile + r]) * scale_log2;
-        // Exponents are taken against the reference max m_ref, which moves only when
-        // the row max grows by more than 2^8; O and l are then scaled by the factor.
+        // Exponents are taken against the running max m_ref; when it grows, O and l are
+        // scaled by exp(m_old - m_new).
         float factor = 1.f;
         if (t == 0) {
           m_ref = mx;  // key 0 of the first tile is never masked: mx is finite
-        } else if (mx > m_ref + kRescaleLog2) {
+        } else if (mx > m_ref) {
           factor = fast_exp2(m_ref - mx);
           m_ref = mx;
         }
-        if (t > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
-          // O must hold P.V of every tile before this one: wait for P.V(G-1), the one
-          // that may still be running (P.V(G-2) completed before S(G) was computed).
-          if (!warp_wait(&s.pv_step, (G - 1) & 1u, &s.abort, 32)) { ok = false; break; }
-          tc_fence_after();
-#pragma unroll 1
-          for (int c = 0; c < D / 32; ++c) {  // this half's D/2 columns, 16 at a time
-            uint32_t w[16];
-            tmem_ld16(o_addr + c * 16, w);
-            tmem_wait_ld();
-            reg_fence<16>(w);
-#pragma unroll
-            for (int k2 = 0; k2 < 16; ++k2) w[k2] = __float_as_uint(__uint_as_float(w[k2]) * factor);
-            tmem_st16(o_addr + c * 16, w);
-          }
-        }
         const float rs = exp_pack64(v, scale_log2, -m_ref);
         tmem_st32(tmem + lane_off + (uint32_t)(b * kTile + hf * 32), v);  // P: bf16 pairs of this half's keys
+        if (t > 0 && __any_sync(0xffffffffu, factor != 1.f)) {
+          // O *= factor before P.V(G) accumulates into it. O must hold P.V of every tile
+          // before this one: wait for P.V(G-1), the one that may still be running
+          // (P.V(G-2) completed before S(G) was computed); by now it usually has. Done
+          // after the P store so the scores' registers can take this half's D/2 O columns
+          // in one TMEM round trip.
+          if (!warp_wait(&s.pv_step, (G - 1) & 1u, &s.abort, 32)) { ok = false; break; }
+          tc_fence_after();
+          tmem_wait_st();  // the P store has read its source registers
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) tmem_ld32(o_addr + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[c * 32]));
+          tmem_wait_ld();
+          reg_fence<D / 2>(v);
+#pragma unroll
+          for (int k2 = 0; k2 < D / 2; ++k2) v[k2] = __float_as_uint(__uint_as_float(v[k2]) * factor);
+#pragma unroll
+          for (int c = 0; c < D / 64; ++c) tmem_st32(o_addr + c * 32, v + c * 32);
+        }
         tmem_wait_st();
         tc_fence_before();
         mbar_arrive(&s.p_full[b]);
@@ -566,21 +568,14 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       const float linv = 1.0f / lt;
       const int qb = uc & 1;  // this unit's Q buffer
       if (un.split) {
-        // Split query tile: this chunk's O / sum in fp16 (a weighted mean of V rows,
-        // rounded 2^-11 relative, far below the bf16 output's 2^-8) and its (max, sum);
+        // Split query tile: this chunk's O / sum in fp32 and its (max, sum);
         // attn_combine_bf16_kernel merges the chunks once this kernel has completed.
-        uint4* op = reinterpret_cast<uint4*>(args.ws + args.ws_o_off) + (size_t)u * (kTile * D / 8) + r;
+        float4* op = reinterpret_cast<float4*>(args.ws + args.ws_o_off) + (size_t)u * (kTile * D / 4) + r;
 #pragma unroll
-        for (int g2 = 0; g2 < D / 16; ++g2) {  // layout [col/8][row][8]: a warp stores 512 contiguous bytes
-          uint32_t hv[4];
-#pragma unroll
-          for (int k2 = 0; k2 < 4; ++k2) {
-            __half2 h2 = __floats2half2_rn(__uint_as_float(w[8 * g2 + 2 * k2]) * linv,
-                                           __uint_as_float(w[8 * g2 + 2 * k2 + 1]) * linv);
-            hv[k2] = *reinterpret_cast<uint32_t*>(&h2);
-          }
-          op[(size_t)(hf * (D / 16) + g2) * kTile] = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        }
+        for (int g4 = 0; g4 < D / 8; ++g4)  // layout [col/4][row][4]: a warp stores 512 contiguous bytes
+          op[(size_t)(hf * (D / 8) + g4) * kTile] =
+              make_float4(__uint_as_float(w[4 * g4]) * linv, __uint_as_float(w[4 * g4 + 1]) * linv,
+                          __uint_as_float(w[4 * g4 + 2]) * linv, __uint_as_float(w[4 * g4 + 3]) * linv);
         if (hf == 0) {
           float* st = reinterpret_cast<float*>(args.ws + args.ws_stats_off) + (size_t)u * 2 * kTile;
           st[r] = m_ref;
@@ -628,7 +623,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
 
 // ------------------------------------------------------------------ split-KV combine
 // A query tile whose key range was split over n_e units has n_e partials: (m_c, l_c) per
-// row and O_c / l_c in fp16. The output row is sum_c w_c (O_c / l_c) / sum_c w_c with
+// row and O_c / l_c in fp32. The output row is sum_c w_c (O_c / l_c) / sum_c w_c with
 // w_c = 2^(m_c - max m) l_c, summed in chunk order so the result does not depend on the
 // schedule. One CTA of 64 threads covers 64 rows x 8 * (8 / NC) columns of one (job,
 // head), so a thread holds 8 partial vectors whatever the chunk count; every
@@ -654,7 +649,7 @@ struct CombineArgs {
 // zeros, so every NC gives the same bits).
 template <int D, int NC>
 __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_constant__ CombineArgs args) {
-  constexpr int GPT = 8 / NC;  // 8-column groups per thread: every thread keeps 8 partial loads in flight
+  constexpr int GPT = 8 / NC;  // 8-column groups per thread: every thread keeps 16 partial loads in flight
   pdl_enter();  // the attention grid before this one has completed and its partials are visible
   const CombineJob jb = args.job[blockIdx.x];
   const int head = blockIdx.y;
@@ -665,8 +660,8 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
   const size_t stride = (size_t)args.heads;  // unit step between consecutive chunks
   const size_t slot0 = (size_t)jb.v0 * args.heads + head;
   const float* stats = reinterpret_cast<const float*>(args.ws + args.ws_stats_off);
-  const uint4* po = reinterpret_cast<const uint4*>(args.ws + args.ws_o_off);
-  uint4 t[NC][GPT];
+  const float4* po = reinterpret_cast<const float4*>(args.ws + args.ws_o_off);
+  float4 t[NC][GPT][2];
   float mc[NC], lc[NC];
 #pragma unroll
   for (int c = 0; c < NC; ++c) {
@@ -676,7 +671,10 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     lc[c] = in ? __ldcg(stats + sl * 2 * kTile + kTile + r) : 0.f;
 #pragma unroll
     for (int g = 0; g < GPT; ++g)
-      t[c][g] = in ? __ldcg(po + sl * (kTile * D / 8) + (size_t)(g0 + g) * kTile + r) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        t[c][g][h] = in ? __ldcg(po + sl * (kTile * D / 4) + (size_t)(2 * (g0 + g) + h) * kTile + r)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   float mmax = -INFINITY;
 #pragma unroll
@@ -694,12 +692,12 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int c = 0; c < NC; ++c) {
-      const __half2* h = reinterpret_cast<const __half2*>(&t[c][g]);
 #pragma unroll
-      for (int k2 = 0; k2 < 4; ++k2) {
-        const float2 x = __half22float2(h[k2]);
-        f[2 * k2] = fmaf(x.x, wc[c], f[2 * k2]);
-        f[2 * k2 + 1] = fmaf(x.y, wc[c], f[2 * k2 + 1]);
+      for (int h = 0; h < 2; ++h) {
+        f[4 * h + 0] = fmaf(t[c][g][h].x, wc[c], f[4 * h + 0]);
+        f[4 * h + 1] = fmaf(t[c][g][h].y, wc[c], f[4 * h + 1]);
+        f[4 * h + 2] = fmaf(t[c][g][h].z, wc[c], f[4 * h + 2]);
+        f[4 * h + 3] = fmaf(t[c][g][h].w, wc[c], f[4 * h + 3]);
       }
     }
 #pragma unroll
@@ -707,6 +705,8 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     dst[g] = pack16<bf16>(f);
   }
 }
+
+#include "attention_pair.cuh"
 
 // ------------------------------------------------------------------ fp32 exact flash kernel
 // CUDA-core flash attention for fp32 inputs (the reference's fp32 tests need 2e-5
@@ -996,7 +996,7 @@ AttnPlan plan_attention(int heads, int kv_group, int seq, int d, bool allow_spli
   if (p.chunk < max_nt) {
     p.stats_off = 0;
     p.o_off = round256((size_t)p.units * 2 * kTile * sizeof(float));
-    p.ws_bytes = p.o_off + (size_t)p.units * kTile * (size_t)d * sizeof(__half);
+    p.ws_bytes = p.o_off + (size_t)p.units * kTile * (size_t)d * sizeof(float);
     int base = 0;  // per-head unit index of each query tile's chunk 0, in decode_unit order
     for (int qt = p.q_tiles - 1; qt >= 0; --qt) {
       const int nc = (qt + p.chunk) / p.chunk;
@@ -1089,6 +1089,212 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid(8), dim3(64), 0, st, "nkl_attention(combine)", ca);
 }
 
+// ---- two-query-tile kernel: plan and launch
+
+struct PairPlan {
+  int pairs = 0, chunk = 0, ctas = 0, units = 0;
+  size_t stats_off = 0, o_off = 0, ws_bytes = 0;  // ws_bytes == 0: no split, no workspace
+  std::vector<uint16_t> cta_off;                  // empty: round-robin over CTAs
+  std::vector<uint4> unit;                        // per listed unit, in cta_off order
+  std::vector<CombineJob> jobs;                   // split query tiles (one job per tile, all heads)
+  int max_chunks = 1;
+};
+
+// Key-tile chunks [j0, j0 + n) of pair p's causal range [0, 2p + 2) for chunk size C,
+// from key tile 0 up; a last chunk of a single key tile (2p + 1, which only tile B uses)
+// is merged into the one before, so every chunk holds key tiles of both query tiles.
+inline int pair_chunks(int p, int C, int* j0 = nullptr, int* n = nullptr) {
+  const int K = 2 * p + 2;
+  int nc = (K + C - 1) / C;
+  if (nc > 1 && K - (nc - 1) * C == 1) --nc;
+  if (j0)
+    for (int c = 0; c < nc; ++c) {
+      j0[c] = c * C;
+      n[c] = c == nc - 1 ? K - c * C : C;
+    }
+  return nc;
+}
+
+// Unit cost in query-tile key steps (tile A's plus tile B's), plus a fixed charge for the
+// unit's Q load, first scores and epilogue; a split plan adds one charge for the
+// combine kernel that follows.
+constexpr long kPairUnitFixed = 4;
+constexpr long kPairCombineCost = 10;
+
+inline long pair_unit_cost(int p, int j0, int n) {
+  const int nA = std::min(n, 2 * p + 1 - j0);
+  return kPairUnitFixed + nA + n;
+}
+
+PairPlan plan_pairs(int heads, int kv_group, int seq, int d, bool allow_split, int sms) {
+  PairPlan plan;
+  const int q_tiles = seq / kTile;
+  plan.pairs = q_tiles / 2;
+  const int P = plan.pairs;
+  const int kmax = 2 * P;
+  struct U { long cost; int head, p, c, j0, n, nc; };
+  auto units_for = [&](int C, std::vector<U>* out) -> long {
+    long count = 0;
+    int j0[kMaxChunks + 2], n[kMaxChunks + 2];
+    for (int p = P - 1; p >= 0; --p) {
+      const int nc = pair_chunks(p, C, j0, n);
+      count += (long)nc * heads;
+      if (out)
+        for (int h = 0; h < heads; ++h)
+          for (int c = 0; c < nc; ++c) out->push_back(U{pair_unit_cost(p, j0[c], n[c]), h, p, c, j0[c], n[c], nc});
+    }
+    return count;
+  };
+  auto lpt = [&](std::vector<U>& us, int ctas, std::vector<std::vector<int>>* lists) -> long {
+    std::stable_sort(us.begin(), us.end(), [](const U& a, const U& b) { return a.cost > b.cost; });
+    std::vector<long> load(ctas, 0);
+    for (int i = 0; i < (int)us.size(); ++i) {
+      int best = 0;
+      for (int b = 1; b < ctas; ++b)
+        if (load[b] < load[best]) best = b;
+      load[best] += us[i].cost;
+      if (lists) (*lists)[best].push_back(i);
+    }
+    return *std::max_element(load.begin(), load.end());
+  };
+  long best_span = -1;
+  int best_c = kmax;
+  const int min_c = std::max(2, (kmax + kMaxChunks - 1) / kMaxChunks);
+  for (int C = kmax; C >= min_c; --C) {
+    if (C < kmax && (!allow_split || 2 * P > kMaxCombineJobs)) break;
+    const long count = units_for(C, nullptr);
+    if (count > kMaxPairSched) break;
+    std::vector<U> us;
+    units_for(C, &us);
+    const int ctas = (int)std::min<long>(count, sms);
+    const long span = lpt(us, ctas, nullptr) + (C < kmax ? kPairCombineCost : 0);
+    if (best_span < 0 || span < best_span) {
+      best_span = span;
+      best_c = C;
+    }
+  }
+  plan.chunk = best_c;
+  const long count = units_for(plan.chunk, nullptr);
+  plan.units = (int)std::min<long>(count, 1L << 30);
+  plan.ctas = (int)std::min<long>(count, sms);
+  if (count > kMaxPairSched || plan.ctas > kMaxCtas) return plan;  // round-robin, no split
+  std::vector<U> us;
+  units_for(plan.chunk, &us);
+  // workspace slots of split pairs: tile A chunk c -> (base + c) * heads + head, tile B
+  // chunk c -> (base + n_e + c) * heads + head, bases in decreasing pair order
+  std::vector<int> base(P, -1);
+  int next = 0;
+  for (int p = P - 1; p >= 0; --p) {
+    const int nc = pair_chunks(p, plan.chunk);
+    if (nc > 1) {
+      base[p] = next;
+      for (int T = 0; T < 2; ++T) {
+        CombineJob j;
+        j.qt = (uint16_t)(2 * p + T);
+        j.v0 = (uint16_t)(next + T * nc);
+        j.n_e = (uint16_t)nc;
+        j.pad = 0;
+        plan.jobs.push_back(j);
+      }
+      plan.max_chunks = std::max(plan.max_chunks, nc);
+      next += 2 * nc;
+    }
+  }
+  std::vector<std::vector<int>> lists(plan.ctas);
+  lpt(us, plan.ctas, &lists);
+  plan.cta_off.assign(1, 0);
+  for (int b = 0; b < plan.ctas; ++b) {
+    for (const int i : lists[b]) {
+      const U& u = us[i];
+      const uint32_t slot = base[u.p] < 0 ? 0xffffffffu : (uint32_t)((base[u.p] + u.c) * heads + u.head);
+      plan.unit.push_back(make_uint4((uint32_t)u.head | ((uint32_t)(u.head / kv_group) << 16),
+                                     (uint32_t)u.p | ((uint32_t)u.j0 << 16), (uint32_t)u.n | ((uint32_t)u.nc << 16),
+                                     slot));
+    }
+    plan.cta_off.push_back((uint16_t)plan.unit.size());
+  }
+  if (next > 0) {
+    const size_t slots = (size_t)next * heads;
+    plan.stats_off = 0;
+    plan.o_off = round256(slots * 2 * kTile * sizeof(float));
+    plan.ws_bytes = plan.o_off + slots * kTile * (size_t)d * sizeof(float);
+  }
+  return plan;
+}
+
+const PairPlan& cached_pair_plan(int heads, int kv_group, int seq, int d, bool allow_split) {
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int, int, bool, int>, PairPlan> cache;
+  const int sms = sm_count();
+  std::lock_guard<std::mutex> lock(mu);
+  auto key = std::make_tuple(heads, kv_group, seq, d, allow_split, sms);
+  auto it = cache.find(key);
+  if (it == cache.end()) it = cache.emplace(key, plan_pairs(heads, kv_group, seq, d, allow_split, sms)).first;
+  return it->second;
+}
+
+// The two-query-tile kernel takes bf16, head_dim 128 and whole 256-row query-tile pairs.
+inline bool pair_kernel_fits(int64_t seq, int64_t d) { return d == 128 && seq % (2 * kTile) == 0; }
+
+template <int D>
+int launch_attn_pair_bf16(const void* q, const void* k, const void* v, void* out, int heads, int kv_heads, int seq,
+                          float scale, void* ws, size_t ws_bytes, const AttnLayout& lay, cudaStream_t st) {
+  CUtensorMap mq, mk, mv, mo;
+  int rc = make_qkv_map(&mq, q, heads, seq, D, lay.q_ss, lay.q_hs, "nkl_attention(q)");
+  if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, lay.k_ss, lay.k_hs, "nkl_attention(k)");
+  if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, lay.v_ss, lay.v_hs, "nkl_attention(v)");
+  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)", 32);
+  if (rc) return rc;
+  const PairPlan& plan = cached_pair_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
+  if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
+    return fail(NKL_ERR_ARG, "nkl_attention_ws: workspace %zu B < required %zu B", ws_bytes, plan.ws_bytes);
+  constexpr size_t smem = pair_smem_bytes<D>();
+  static std::atomic<bool> attr_set[64] = {};  // per device: the smem attribute is set (idempotent)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
+    cudaError_t e =
+        cudaFuncSetAttribute(attn_fwd_pair_bf16_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_attention: %s", cudaGetErrorString(e));
+    if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
+  }
+  static PairArgs a;  // large kernel-parameter block, filled under the lock below
+  static std::mutex a_mu;
+  std::lock_guard<std::mutex> lock(a_mu);
+  a.ws = plan.ws_bytes > 0 ? static_cast<unsigned char*>(ws) : nullptr;
+  a.heads = heads;
+  a.pairs = plan.pairs;
+  a.kv_group = heads / kv_heads;
+  a.seq = seq;
+  a.scale_log2 = scale * kLog2e;
+  a.ws_stats_off = plan.stats_off;
+  a.ws_o_off = plan.o_off;
+  a.n_ctas_listed = plan.cta_off.empty() ? 0 : plan.ctas;
+  a.units = plan.units;
+  std::copy(plan.cta_off.begin(), plan.cta_off.end(), a.cta_off);
+  std::copy(plan.unit.begin(), plan.unit.end(), a.unit);
+  rc = launch_pdl(attn_fwd_pair_bf16_kernel<D>, dim3(plan.ctas), dim3(kPairThreads), smem, st, "nkl_attention", mq,
+                  mk, mv, mo, a);
+  if (rc || plan.jobs.empty()) return rc;
+  static CombineArgs ca;
+  ca.ws = static_cast<const unsigned char*>(ws);
+  ca.out = static_cast<bf16*>(out);
+  ca.heads = heads;
+  ca.seq = seq;
+  ca.n_jobs = (int)plan.jobs.size();
+  ca.ws_stats_off = plan.stats_off;
+  ca.ws_o_off = plan.o_off;
+  ca.o_ss = lay.o_ss;
+  ca.o_hs = lay.o_hs;
+  std::copy(plan.jobs.begin(), plan.jobs.end(), ca.job);
+  auto grid = [&](int nc) { return dim3((unsigned)plan.jobs.size(), (unsigned)heads, (unsigned)(2 * (D / 8) / (8 / nc))); };
+  if (plan.max_chunks <= 2)
+    return launch_pdl(attn_combine_bf16_kernel<D, 2>, grid(2), dim3(64), 0, st, "nkl_attention(combine)", ca);
+  if (plan.max_chunks <= 4)
+    return launch_pdl(attn_combine_bf16_kernel<D, 4>, grid(4), dim3(64), 0, st, "nkl_attention(combine)", ca);
+  return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid(8), dim3(64), 0, st, "nkl_attention(combine)", ca);
+}
+
 int check_attn(const char* op, int64_t heads, int64_t seq, int64_t d, int dtype) {
   if (!valid_dtype(dtype)) return fail(NKL_ERR_DTYPE, "%s: unsupported dtype %d", op, dtype);
   if (heads < 0 || seq < 0 || d < 1 || d > 128)
@@ -1118,7 +1324,8 @@ namespace {
 // one unit.
 int attention_impl(const char* op, const void* q, const void* k, const void* v, void* out, void* workspace,
                    size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq, int64_t head_dim,
-                   float scale, int dtype, void* stream, const AttnLayout* layout = nullptr) {
+                   float scale, int dtype, void* stream, const AttnLayout* layout = nullptr,
+                   int mode = NKL_ATTN_AUTO) {
   int rc = check_attn(op, heads, seq, head_dim, dtype);
   if (rc) return rc;
   if (heads == 0 || seq == 0) return NKL_OK;
@@ -1143,6 +1350,14 @@ int attention_impl(const char* op, const void* q, const void* k, const void* v, 
   if (!is_aligned(q, 16) || !is_aligned(k, 16) || !is_aligned(v, 16) || !is_aligned(out, 16))
     return fail(NKL_ERR_ALIGN, "%s: bf16 tensors must be 16-byte aligned", op);
   if (workspace && !is_aligned(workspace, 256)) return fail(NKL_ERR_ALIGN, "%s: workspace not 256-byte aligned", op);
+  if (mode == NKL_ATTN_TWO_TILE) {
+    if (!pair_kernel_fits(seq, head_dim))
+      return fail(NKL_ERR_SHAPE, "%s: the two-query-tile kernel needs head_dim 128 and seq %% 256 == 0 (got %lld, %lld)",
+                  op, (long long)head_dim, (long long)seq);
+    return launch_attn_pair_bf16<128>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
+                                      workspace ? workspace_bytes : 0, lay, st);
+  }
+  if (mode == NKL_ATTN_ONE_TILE_UNSPLIT) workspace = nullptr;
   if (head_dim == 64)
     return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
                                 workspace ? workspace_bytes : 0, lay, st);
@@ -1237,4 +1452,24 @@ extern "C" int nkl_attention_naive(const void* q, const void* k, const void* v, 
                                                             S, 1.f);
   }
   return check_launch("nkl_attention_naive");
+}
+
+extern "C" size_t nkl_attention_mode_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype, int mode) {
+  if (mode == NKL_ATTN_ONE_TILE_UNSPLIT) return 0;
+  if (mode != NKL_ATTN_TWO_TILE) return nkl_attention_workspace_size(heads, seq, head_dim, dtype);
+  if (dtype != NKL_BFLOAT16 || heads <= 0 || heads > 65535 || seq <= 0 || seq > (1 << 24) ||
+      !pair_kernel_fits(seq, head_dim))
+    return 0;
+  return cached_pair_plan((int)heads, 1, (int)seq, (int)head_dim, true).ws_bytes;
+}
+
+extern "C" int nkl_attention_mode(const void* q, const void* k, const void* v, void* out, void* workspace,
+                                  size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim, float scale,
+                                  int dtype, int mode, void* stream) {
+  if (mode != NKL_ATTN_AUTO && mode != NKL_ATTN_ONE_TILE_UNSPLIT && mode != NKL_ATTN_TWO_TILE)
+    return fail(NKL_ERR_ARG, "nkl_attention_mode: unknown mode %d", mode);
+  if (mode == NKL_ATTN_TWO_TILE && dtype != NKL_BFLOAT16)
+    return fail(NKL_ERR_DTYPE, "nkl_attention_mode: the two-query-tile kernel is bf16 only");
+  return attention_impl("nkl_attention_mode", q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr,
+                        workspace_bytes, heads, heads, seq, head_dim, scale, dtype, stream, nullptr, mode);
 }

@@ -67,13 +67,15 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // of 128 (see nkl_matmul_swiglu) and writes silu(gate) * up, each rounded to bf16 first
 // exactly as the unfused matmul -> swiglu path rounds them, into C[M, N/2]. kEpiResidual
 // writes C = R + A.B with A.B rounded to bf16 first and the sum rounded once more, as a
-// bf16 matmul followed by a bf16 add rounds it.
-constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2;
+// bf16 matmul followed by a bf16 add rounds it. kEpiF32 writes the fp32 accumulator
+// unrounded into a float C (the partial products of a tensor-parallel layer, summed
+// across GPUs before their one rounding).
+constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2, kEpiF32 = 3;
 
 template <int BN, int STAGES, int EPI = kEpiStore>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                    bf16* __restrict__ c, const bf16* __restrict__ res, int M, int N, int K, int m_tiles,
+                    void* __restrict__ c_out, const bf16* __restrict__ res, int M, int N, int K, int m_tiles,
                     int n_tiles) {
   extern __shared__ uint8_t smem_raw[];
   pdl_launch_dependents();
@@ -87,6 +89,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  bf16* const c = static_cast<bf16*>(c_out);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -244,6 +247,26 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
         mbar_arrive(&s.acc_empty[acc]);
         continue;
       }
+      if constexpr (EPI == kEpiF32) {
+        float* frow = static_cast<float*>(c_out) + (int64_t)gm * N;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tmem + (uint32_t)(acc * BN + cc * 32) + ((uint32_t)(q * 32) << 16), r);
+          tmem_wait_ld();
+          const int gn = nt * BN + cc * 32;
+          if (gm < M) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)  // N % 8 == 0: a 4-column group is all in range or all out
+              if (gn + v * 4 < N)
+                *reinterpret_cast<uint4*>(frow + gn + v * 4) =
+                    make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s.acc_empty[acc]);
+        continue;
+      }
       bf16* crow = c + (int64_t)gm * N;
       const bf16* rrow = EPI == kEpiResidual ? res + (int64_t)gm * N : nullptr;
 #pragma unroll 1
@@ -379,7 +402,7 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
     if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
   return launch_pdl(gemm_bf16_tc_kernel<BN, STAGES, EPI>, dim3(grid), dim3(kGemmThreads), smem, st, "nkl_matmul", ma,
-                    mb, static_cast<bf16*>(c), static_cast<const bf16*>(res), M, N, K, m_tiles, n_tiles);
+                    mb, c, static_cast<const bf16*>(res), M, N, K, m_tiles, n_tiles);
 }
 
 // Tile width by how many tiles the SMs get. 256-column tiles read 96 B/clk of MMA
@@ -456,6 +479,26 @@ extern "C" int nkl_matmul_residual(const void* a, const void* b, const void* res
   if (!is_aligned(a, 16) || !is_aligned(b, 16) || !is_aligned(residual, 16) || !is_aligned(out, 16))
     return fail(NKL_ERR_ALIGN, "nkl_matmul_residual: operands must be 16-byte aligned");
   return dispatch_tc<kEpiResidual>(a, b, out, residual, M, N, K, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int nkl_matmul_f32out(const void* a, const void* b, float* c, int64_t M, int64_t N, int64_t K,
+                                 int dtype, void* stream) {
+  int rc = check_gemm("nkl_matmul_f32out", M, N, K, dtype);
+  if (rc) return rc;
+  if (dtype != NKL_BFLOAT16) return fail(NKL_ERR_DTYPE, "nkl_matmul_f32out: bf16 inputs only");
+  if (M == 0 || N == 0) return NKL_OK;
+  if (!a || !b || !c) return fail(NKL_ERR_ARG, "nkl_matmul_f32out: NULL pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    cudaError_t e = cudaMemsetAsync(c, 0, (size_t)M * (size_t)N * sizeof(float), st);
+    return e == cudaSuccess ? NKL_OK : fail(NKL_ERR_CUDA, "nkl_matmul_f32out: %s", cudaGetErrorString(e));
+  }
+  if (K % 8 != 0 || N % 8 != 0)
+    return fail(NKL_ERR_SHAPE, "nkl_matmul_f32out: needs K and N multiples of 8 (got K=%lld N=%lld)", (long long)K,
+                (long long)N);
+  if (!is_aligned(a, 16) || !is_aligned(b, 16) || !is_aligned(c, 16))
+    return fail(NKL_ERR_ALIGN, "nkl_matmul_f32out: operands must be 16-byte aligned");
+  return dispatch_tc<kEpiF32>(a, b, c, nullptr, M, N, K, st);
 }
 
 extern "C" int nkl_matmul_swiglu(const void* a, const void* b_gate_up, void* out, int64_t M, int64_t F, int64_t K,

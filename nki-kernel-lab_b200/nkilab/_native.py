@@ -16,6 +16,11 @@ LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), LIB_NAME)
 FLOAT32 = 0
 BFLOAT16 = 1
 
+# attention launch modes (NKL_ATTN_*)
+ATTN_AUTO = 0
+ATTN_ONE_TILE_UNSPLIT = 1
+ATTN_TWO_TILE = 2
+
 # status codes (nkl_status)
 OK = 0
 ERR_SHAPE = 1
@@ -49,12 +54,15 @@ SIGNATURES = {
     "nkl_matmul_naive": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_swiglu": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_matmul_residual": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _int, _p]),
+    "nkl_matmul_f32out": (_int, [_p, _p, _p, _i64, _i64, _i64, _int, _p]),
     "nkl_attention": (_int, [_p, _p, _p, _p, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_workspace_size": (_sz, [_i64, _i64, _i64, _int]),
     "nkl_attention_ws": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_strided": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                                      _i64, _f, _int, _p]),
     "nkl_attention_gqa": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _f, _int, _p]),
+    "nkl_attention_mode_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
+    "nkl_attention_mode": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _int, _p]),
     "nkl_attention_naive_workspace_size": (_sz, [_i64, _i64, _int]),
     "nkl_attention_naive": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
 }

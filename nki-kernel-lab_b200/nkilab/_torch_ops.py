@@ -8,6 +8,7 @@ compose with streams and CUDA-graph capture like any torch op:
     torch.ops.nkilab.softmax(x, fused)              -> nkl_softmax / nkl_softmax_unfused
     torch.ops.nkilab.swiglu(gate, up)               -> nkl_swiglu
     torch.ops.nkilab.matmul(a, b, naive)            -> nkl_matmul / nkl_matmul_naive
+    torch.ops.nkilab.matmul_f32out(a, b)            -> nkl_matmul_f32out (bf16 in, fp32 out)
     torch.ops.nkilab.attention(q, k, v, scale, naive) -> nkl_attention_ws / nkl_attention_naive
 
 There is no CPU implementation: a CPU tensor is an error, never a fallback.
@@ -210,6 +211,25 @@ def matmul_residual(a: torch.Tensor, b: torch.Tensor, residual: torch.Tensor) ->
 @matmul_residual.register_fake
 def _(a, b, residual):
     return a.new_empty((a.shape[0], b.shape[1]))
+
+
+@torch.library.custom_op("nkilab::matmul_f32out", mutates_args=())
+def matmul_f32out(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """a @ b for bf16 a, b with the fp32 accumulator returned unrounded (float32 [M, N])."""
+    dev, dt, st = _prep(a, b)
+    M, K = a.shape
+    K2, Ncols = b.shape
+    if K != K2:
+        raise ValueError(f"inner dimensions differ: {tuple(a.shape)} @ {tuple(b.shape)}")
+    out = torch.empty((M, Ncols), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        N.call("nkl_matmul_f32out", a.data_ptr(), b.data_ptr(), out.data_ptr(), M, Ncols, K, dt, st)
+    return out
+
+
+@matmul_f32out.register_fake
+def _(a, b):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=torch.float32)
 
 
 # Split-KV workspaces of the bf16 attention kernel. Eager calls share one workspace per

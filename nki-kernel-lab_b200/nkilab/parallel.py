@@ -52,6 +52,10 @@ def all_gather_dim0(local: torch.Tensor, n_total: int, group=None) -> torch.Tens
         return local
     sizes = [shard_range(n_total, world, r) for r in range(world)]
     max_rows = max(e - s for s, e in sizes)
+    if n_total % world == 0:  # even shards: gather straight into the result
+        out = torch.empty((n_total,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+        return out
     if local.shape[0] != max_rows:
         pad = torch.zeros((max_rows - local.shape[0],) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
         local = torch.cat([local, pad], 0)
@@ -71,6 +75,10 @@ def reduce_scatter_dim0(full: torch.Tensor, group=None) -> torch.Tensor:
     sizes = [shard_range(n, world, r) for r in range(world)]
     max_rows = max(e - s for s, e in sizes)
     acc = full.float() if full.dtype == torch.bfloat16 else full
+    if n % world == 0:  # even shards: scatter straight from the input
+        out = torch.empty((n // world,) + tuple(acc.shape[1:]), dtype=acc.dtype, device=acc.device)
+        dist.reduce_scatter_tensor(out, acc.contiguous(), op=dist.ReduceOp.SUM, group=group)
+        return out.to(full.dtype)
     chunks = []
     for s, e in sizes:
         c = acc[s:e]
@@ -96,11 +104,19 @@ def _default_attention(q, k, v, variant):
 def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, variant: str = "flash_pipelined", group=None,
               compute: Optional[Callable] = None) -> torch.Tensor:
     """Head-sharded causal attention. q, k, v: [H, S, d], the same full tensors on
-    every rank (or only this rank's head rows are read). Returns the full [H, S, d]
-    output on every rank after one all-gather."""
+    every rank (only this rank's head rows are read). Returns the full [H, S, d]
+    output on every rank after one all-gather. With the default compute, q, k, v may
+    be CPU tensors (pinned for asynchronous copies): only this rank's heads are copied
+    to the current GPU, and the gathered output comes back on the CPU, as
+    nkilab.ops.attention returns host input's result on the host."""
     world, rank = _world(group)
     H = q.shape[0]
     h0, h1 = shard_range(H, world, rank)
+    if compute is None and q.device.type == "cpu":
+        from ._host import like_input, to_device
+
+        local = _default_attention(*(to_device(t[h0:h1]) for t in (q, k, v)), variant)
+        return like_input(all_gather_dim0(local, H, group), q)
     fn = compute or _default_attention
     local = fn(q[h0:h1].contiguous(), k[h0:h1].contiguous(), v[h0:h1].contiguous(), variant)
     return all_gather_dim0(local, H, group)
@@ -158,6 +174,9 @@ def matmul(a: torch.Tensor, b: torch.Tensor, group=None, compute: Optional[Calla
 
 # --------------------------------------------------------------------------- decoder block
 
+FF_UNIT = 128  # FFN columns are sharded in units of 128 (the fused SwiGLU GEMM's column block)
+
+
 @dataclass
 class ShardedBlockWeights:
     """This rank's slice of a DecoderBlock, transposed to [in, out] for x @ W."""
@@ -170,30 +189,44 @@ class ShardedBlockWeights:
     wd: torch.Tensor     # [local_ff, d]
     heads: tuple[int, int]
     ff: tuple[int, int]
+    wgu: Optional[torch.Tensor] = None  # [d, 2 * local_ff] gate/up interleaved for the fused SwiGLU GEMM
+
+
+def ff_range(d_ff: int, world: int, rank: int) -> tuple[int, int]:
+    """[start, end) of rank's FFN columns: whole 128-column units, as even as possible."""
+    units = (d_ff + FF_UNIT - 1) // FF_UNIT
+    u0, u1 = shard_range(units, world, rank)
+    return min(u0 * FF_UNIT, d_ff), min(u1 * FF_UNIT, d_ff)
 
 
 def shard_block(block, world: int, rank: int, dtype: torch.dtype, device) -> ShardedBlockWeights:
+    """Slice `block`'s weights for `rank` of `world`: heads by shard_range, FFN columns by
+    ff_range. The weights may live on any device; the slices are moved to `device`."""
     cfg = block.cfg
     d, H, hd = cfg.d_model, cfg.n_heads, cfg.head_dim
     h0, h1 = shard_range(H, world, rank)
-    f0, f1 = shard_range(cfg.d_ff, world, rank)
+    f0, f1 = ff_range(cfg.d_ff, world, rank)
     with torch.no_grad():
         wqkv = block.wqkv.weight.detach()  # [3d, d]: q rows, then k, then v
         cols = [wqkv[i * d + h0 * hd:i * d + h1 * hd] for i in range(3)]
 
         def t(w):
-            return w.t().contiguous().to(device=device, dtype=dtype)
+            return w.t().to(device=device, dtype=dtype).contiguous()
 
-        return ShardedBlockWeights(
-            norm1=block.norm1.weight.detach().to(device=device, dtype=dtype),
-            norm2=block.norm2.weight.detach().to(device=device, dtype=dtype),
+        sw = ShardedBlockWeights(
+            norm1=block.norm1.weight.detach().to(device=device, dtype=dtype).contiguous(),
+            norm2=block.norm2.weight.detach().to(device=device, dtype=dtype).contiguous(),
             wqkv=t(torch.cat(cols, 0)),
             wo=t(block.wo.weight.detach()[:, h0 * hd:h1 * hd]),
             wg=t(block.wg.weight.detach()[f0:f1]),
             wu=t(block.wu.weight.detach()[f0:f1]),
             wd=t(block.wd.weight.detach()[:, f0:f1]),
             heads=(h0, h1), ff=(f0, f1))
+        if (dtype == torch.bfloat16 and sw.wg.is_cuda and f1 > f0 and (f1 - f0) % FF_UNIT == 0):
+            from . import _torch_ops
 
+            sw.wgu = _torch_ops.interleave_gate_up(sw.wg, sw.wu)
+        return sw
 
 
 def _device_ops():
@@ -201,45 +234,110 @@ def _device_ops():
 
     return ops
 
+
+class _Marks:
+    """CUDA events recorded at the block's phase boundaries (for the bench's breakdown)."""
+
+    def __init__(self, record: Optional[list]):
+        self.record = record
+
+    def __call__(self, name: str) -> None:
+        if self.record is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.record.append((name, ev))
+
+
 def decoder_block(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights] = None,
-                  variant: str = "flash_pipelined", group=None, ops_module=None) -> torch.Tensor:
-    """Tensor-parallel DecoderBlock forward. x: [S, d] full input on every rank.
-    Returns the full [S, d] output on every rank."""
+                  variant: str = "flash_pipelined", group=None, ops_module=None,
+                  marks: Optional[list] = None) -> torch.Tensor:
+    """Tensor-parallel DecoderBlock forward (nkilab/model.py:70-89, sharded).
+
+    x: [S, d] or [B, S, d], the same full input on every rank (only this rank's row block
+    of the flattened [B * S, d] rows is read). Returns the full output on every rank.
+
+    Heads and FFN columns are split over the ranks, rows (sequence parallel) for the norms
+    and residual adds. Per block: RMSNorm of the local rows -> all-gather -> QKV and causal
+    attention of the local heads (per batch element) -> Wo partial in fp32 ->
+    reduce-scatter (fp32 sum over ranks, one rounding to x's dtype: the rounding point of
+    the single-GPU Wo product) -> residual add + RMSNorm of the local rows -> all-gather ->
+    gate/up + SwiGLU of the local FFN columns -> Wd partial in fp32 -> reduce-scatter ->
+    residual add -> all-gather of the block output. On CUDA bf16 the block uses the same
+    fused kernels as the one-GPU path (strided attention over the QKV projection, fused
+    residual add + RMSNorm, gate/up GEMM with SwiGLU in its epilogue) and fp32-output GEMMs
+    for the partials. `marks`, if a list, receives (name, CUDA event) pairs at the phase
+    boundaries."""
     world, rank = _world(group)
+    dev_ops = ops_module is None
     if ops_module is None:
         from . import ops as ops_module
+    mark = _Marks(marks)
     cfg = block.cfg
-    S, d = x.shape
+    lead = x.shape[:-1]
+    S, d = x.shape[-2], x.shape[-1]
+    B = x[..., 0, 0].numel() if x.dim() == 3 else 1
+    R = B * S
     hd = cfg.head_dim
-    w = weights or shard_block(block, world, rank, x.dtype, x.device)
+    dt = x.dtype
+    w = weights or shard_block(block, world, rank, dt, x.device)
     nh = w.heads[1] - w.heads[0]
-    r0, r1 = shard_range(S, world, rank)
-    x_loc = x[r0:r1]
-    # attention half: norm on local rows -> gather rows -> local heads -> partial Wo -> reduce-scatter
-    h = all_gather_dim0(ops_module.rmsnorm(x_loc.contiguous(), w.norm1, cfg.eps), S, group)
+    r0, r1 = shard_range(R, world, rank)
+    x_loc = x.reshape(R, d)[r0:r1].contiguous()
+    fused = dev_ops and x.is_cuda and dt == torch.bfloat16
+
+    def partial_f32(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+        if fused:
+            return torch.ops.nkilab.matmul_f32out(a.contiguous(), b)
+        f32 = getattr(ops_module, "matmul_f32", None)
+        return f32(a, b) if f32 is not None else ops_module.matmul(a, b).float()
+
+    # ---- attention half
+    mark("start")
+    h_loc = ops_module.rmsnorm(x_loc, w.norm1, cfg.eps)
+    mark("norm1")
+    h = all_gather_dim0(h_loc, R, group)
+    mark("all_gather_1")
     if nh > 0:
-        qkv = ops_module.matmul(h, w.wqkv)
-        if (ops_module is _device_ops() and qkv.is_cuda and qkv.dtype == torch.bfloat16 and variant != "naive"
-                and hd in (64, 128)):
-            # local heads read straight out of the projection, output in the Wo layout
-            a = torch.empty(S, nh, hd, dtype=qkv.dtype, device=qkv.device)
-            q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].view(S, nh, hd).transpose(0, 1) for i in range(3))
-            torch.ops.nkilab.attention_strided_(q, k, v, a.transpose(0, 1), 1.0 / math.sqrt(hd))
-            part = ops_module.matmul(a.view(S, nh * hd), w.wo)
+        qkv = ops_module.matmul(h, w.wqkv)  # [R, 3 * nh * hd]
+        if fused and variant != "naive" and hd in (64, 128):
+            a = torch.empty(R, nh * hd, dtype=dt, device=x.device)
+            qkv3 = qkv.view(B, S, 3, nh, hd)
+            a3 = a.view(B, S, nh, hd)
+            for b in range(B):  # local heads read straight out of the projection, output in the Wo layout
+                q, k, v = (qkv3[b, :, i].transpose(0, 1) for i in range(3))
+                torch.ops.nkilab.attention_strided_(q, k, v, a3[b].transpose(0, 1), 1.0 / math.sqrt(hd))
         else:
-            q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].reshape(S, nh, hd).transpose(0, 1).contiguous()
-                       for i in range(3))
+            q, k, v = (qkv[:, i * nh * hd:(i + 1) * nh * hd].reshape(B, S, nh, hd).permute(0, 2, 1, 3)
+                       .reshape(B * nh, S, hd).contiguous() for i in range(3))
             a = ops_module.attention(q, k, v, variant=variant)
-            part = ops_module.matmul(a.transpose(0, 1).reshape(S, nh * hd).contiguous(), w.wo)
+            a = a.view(B, nh, S, hd).permute(0, 2, 1, 3).reshape(R, nh * hd).contiguous()
+        part = partial_f32(a, w.wo)
     else:
-        part = torch.zeros((S, d), dtype=x.dtype, device=x.device)
-    x_loc = (x_loc.float() + reduce_scatter_dim0(part, group).float()).to(x.dtype)
-    # MLP half: norm on local rows -> gather rows -> local FFN columns -> partial Wd -> reduce-scatter
-    h = all_gather_dim0(ops_module.rmsnorm(x_loc.contiguous(), w.norm2, cfg.eps), S, group)
+        part = torch.zeros((R, d), dtype=torch.float32, device=x.device)
+    mark("attention")
+    attn_out = reduce_scatter_dim0(part, group).to(dt)  # fp32 sum over ranks, one rounding
+    mark("reduce_scatter_1")
+    if fused:
+        x_loc, h_loc = torch.ops.nkilab.add_rmsnorm(x_loc, attn_out.contiguous(), w.norm2, cfg.eps)
+    else:
+        x_loc = (x_loc.float() + attn_out.float()).to(dt)
+        h_loc = ops_module.rmsnorm(x_loc, w.norm2, cfg.eps)
+    mark("norm2")
+    # ---- MLP half
+    h = all_gather_dim0(h_loc, R, group)
+    mark("all_gather_2")
     if w.ff[1] > w.ff[0]:
-        act = ops_module.swiglu(ops_module.matmul(h, w.wg), ops_module.matmul(h, w.wu))
-        part = ops_module.matmul(act, w.wd)
+        if fused and w.wgu is not None:
+            act = torch.ops.nkilab.matmul_swiglu(h, w.wgu)
+        else:
+            act = ops_module.swiglu(ops_module.matmul(h, w.wg), ops_module.matmul(h, w.wu))
+        part = partial_f32(act, w.wd)
     else:
-        part = torch.zeros((S, d), dtype=x.dtype, device=x.device)
-    x_loc = (x_loc.float() + reduce_scatter_dim0(part, group).float()).to(x.dtype)
-    return all_gather_dim0(x_loc, S, group)
+        part = torch.zeros((R, d), dtype=torch.float32, device=x.device)
+    mark("mlp")
+    mlp_out = reduce_scatter_dim0(part, group).to(dt)
+    mark("reduce_scatter_2")
+    y_loc = (x_loc.float() + mlp_out.float()).to(dt)
+    out = all_gather_dim0(y_loc, R, group)
+    mark("all_gather_3")
+    return out.view(*lead, d)

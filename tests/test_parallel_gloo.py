@@ -36,7 +36,8 @@ def _oracle_ops():
     def attention(q, k, v, variant="flash_pipelined"):
         return (O.attention_naive if variant == "naive" else O.attention_flash)(q, k, v)
 
-    return types.SimpleNamespace(rmsnorm=O.rmsnorm, matmul=O.matmul, swiglu=O.swiglu, attention=attention)
+    return types.SimpleNamespace(rmsnorm=O.rmsnorm, matmul=O.matmul, swiglu=O.swiglu, attention=attention,
+                                 matmul_f32=lambda a, b: a.float() @ b.float())
 
 
 def _row_compute(op, *args, **kw):
@@ -99,6 +100,17 @@ def _worker_block(rank, world, port):
         out = P.decoder_block(block, x, ops_module=_oracle_ops())
         assert out.shape == x.shape
         assert float((out - ref).abs().max()) < 1e-5, float((out - ref).abs().max())
+        # batched input [B, S, d]: rows of all batch elements are sharded together, attention
+        # stays within each element; the phase marks come back in order
+        xb = torch.randn(3, 40, 256, generator=torch.Generator().manual_seed(2))
+        with torch.no_grad():
+            refb = torch.stack([block(xb[i]) for i in range(3)])
+        outb = P.decoder_block(block, xb, ops_module=_oracle_ops())
+        assert outb.shape == xb.shape
+        assert float((outb - refb).abs().max()) < 1e-5, float((outb - refb).abs().max())
+        # FFN columns in whole 128-column units: d_ff=1000 -> 8 units, 4 per rank
+        f0, f1 = P.ff_range(1000, world, rank)
+        assert (f0, f1) == ((0, 512) if rank == 0 else (512, 1000))
     finally:
         dist.destroy_process_group()
 
