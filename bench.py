@@ -66,11 +66,13 @@ def peaks() -> dict:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
-def ncu_traffic(kernel_file: str):
-    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<kernel_file>."""
+def ncu_traffic(kernel_file: str, key: str = ""):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<kernel_file>: the
+    line 'traffic_bytes_per_launch[ key]: N'."""
     try:
         with open(os.path.join(ROOT, "profiles", kernel_file)) as f:
-            m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read())
+            pat = r"traffic_bytes_per_launch" + (r"\s+" + re.escape(key) if key else "") + r":\s*([0-9.eE+]+)"
+            m = re.search(pat, f.read())
         return float(m.group(1)) if m else None
     except OSError:
         return None
@@ -320,6 +322,7 @@ def bench_rows(steps: int, warmup: int, dev, stream, pk) -> dict:
         gbs = alg_bytes / (ms * 1e-3) / 1e9
         sp = spread(runs, steps)
         out[name] = {"us": round(ms * 1e3, 3), "gbs": round(gbs, 1), "frac": round(gbs / pk["hbm_gbs"], 4),
+                     "traffic_bytes_per_launch": ncu_traffic("rows_bf16_4096x2048.md", name),
                      "frac_min": round(alg_bytes / (sp["max"] * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
                      "frac_max": round(alg_bytes / (sp["min"] * 1e-6) / 1e9 / pk["hbm_gbs"], 4),
                      "us_spread": sp, "bytes_per_launch": alg_bytes, "pool_mib": round(nset * alg_bytes / 2**20),
@@ -341,10 +344,18 @@ def bench_gemm(dev, stream, pk) -> dict:
             a, b = sets[i % len(sets)]
             torch.ops.nkilab.matmul(a, b, False)
 
+        def cublas(i, sets=sets):
+            a, b = sets[i % len(sets)]
+            torch.matmul(a, b)
+
         warm(step, 3, stream)
         ms = timed_graph(step, steps, stream) / steps
+        warm(cublas, 3, stream)
+        ms_cublas = timed_graph(cublas, steps, stream) / steps  # the library GEMM, same inputs and harness
         tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
-        out[f"{n}^3"] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / pk["bf16_tflops"], 4)}
+        out[f"{n}^3"] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / pk["bf16_tflops"], 4),
+                         "cublas_us_same_run": round(ms_cublas * 1e3, 2),
+                         "traffic_bytes_per_launch": ncu_traffic("gemm_bf16_tc_1024_8192.md", str(n))}
         del sets
     return out
 
@@ -438,6 +449,85 @@ def bench_block(dev, stream, pk, ctx) -> dict:
     out.update({"ms": round(ms, 3), "tflops": round(tf, 1),
                 "frac": round(tf / (world * pk["bf16_tflops_sustained"]), 4)})
     del block
+    return out
+
+
+def bench_ladder(dev, stream, pk) -> dict:
+    """The reference's variant ladder (README.md:17-23, bench/run_bench.py:108-138) as
+    measured B200 rungs, each a distinct kernel or launch mode, graph-timed like the
+    headline (median of 7 replays, rotating inputs larger than L2):
+      attention 8x2048x128: naive (scores and probabilities through HBM) -> flash, one
+      query tile per CTA, no split (flash / flash_kv_resident) -> the same kernel with
+      causal key ranges split over all SMs (flash_balanced; the default) -> two query
+      tiles per CTA interleaved (flash_pipelined's ILP = 2)
+      softmax [4096, 2048]: unfused (3 HBM passes) -> fused; GEMM 1024^3: naive -> blocked."""
+    from nkilab import _native as N
+
+    out = {}
+    scale = 1.0 / math.sqrt(D)
+    per = 4 * H * S * D * 2
+    nset = max(2, math.ceil(POOL_BYTES / per))
+    g = torch.Generator(device=dev).manual_seed(21)
+    sets = [[torch.randn(H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(4)] for _ in range(nset)]
+    st = stream.cuda_stream
+    att = {}
+    for name, mode in (("flash_one_tile_unsplit", N.ATTN_ONE_TILE_UNSPLIT), ("flash_split_kv_default", N.ATTN_AUTO),
+                       ("flash_two_tile", N.ATTN_TWO_TILE)):
+        nbytes = N.lib.nkl_attention_mode_workspace_size(H, S, D, N.BFLOAT16, mode)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+
+        def step(i, mode=mode, ws=ws, nbytes=nbytes):
+            q, k, v, o = sets[i % nset]
+            N.call("nkl_attention_mode", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), ws.data_ptr(), nbytes,
+                   H, S, D, scale, N.BFLOAT16, mode, st)
+
+        warm(step, 3, stream)
+        us = statistics.median(timed_graph_runs(step, 20, stream)) / 20 * 1e3
+        att[name] = {"us": round(us, 2), "tflops": round(ATTN_FLOP / (us * 1e-6) / 1e12, 1)}
+    nb = N.lib.nkl_attention_naive_workspace_size(H, S, N.BFLOAT16)
+    wsn = torch.empty(nb, dtype=torch.uint8, device=dev)
+
+    def naive(i):
+        q, k, v, o = sets[i % nset]
+        N.call("nkl_attention_naive", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), wsn.data_ptr(), nb, H, S,
+               D, scale, N.BFLOAT16, st)
+
+    warm(naive, 2, stream)
+    us = statistics.median(timed_graph_runs(naive, 3, stream, replays=3)) / 3 * 1e3
+    att = {"naive": {"us": round(us, 1), "tflops": round(ATTN_FLOP / (us * 1e-6) / 1e12, 2)}, **att}
+    del wsn, sets
+    out["attention_8x2048x128"] = att
+    x = [torch.randn(ROWS, COLS, device=dev, generator=g).to(torch.bfloat16) for _ in range(8)]
+    y = torch.empty_like(x[0])
+    wb = N.lib.nkl_softmax_unfused_workspace_size(ROWS, COLS)
+    wsu = torch.empty(wb, dtype=torch.uint8, device=dev)
+    sm = {}
+    for name in ("unfused", "fused"):
+        def step(i, name=name):
+            t = x[i % len(x)]
+            if name == "fused":
+                N.call("nkl_softmax", t.data_ptr(), y.data_ptr(), ROWS, COLS, N.BFLOAT16, st)
+            else:
+                N.call("nkl_softmax_unfused", t.data_ptr(), y.data_ptr(), wsu.data_ptr(), wb, ROWS, COLS, N.BFLOAT16, st)
+
+        warm(step, 3, stream)
+        us = statistics.median(timed_graph_runs(step, 20, stream)) / 20 * 1e3
+        sm[name] = {"us": round(us, 2), "gbs_algorithmic": round(2 * ROWS * COLS * 2 / (us * 1e-6) / 1e9, 1)}
+    out["softmax_4096x2048"] = sm
+    del x, wsu
+    n = 1024
+    mats = [[(torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(torch.bfloat16) for _ in range(3)] for _ in range(16)]
+    gm = {}
+    for name in ("naive", "blocked"):
+        def step(i, name=name):
+            a, b, c = mats[i % len(mats)]
+            N.call("nkl_matmul_naive" if name == "naive" else "nkl_matmul", a.data_ptr(), b.data_ptr(), c.data_ptr(), n, n,
+                   n, N.BFLOAT16, st)
+
+        warm(step, 3, stream)
+        us = statistics.median(timed_graph_runs(step, 10, stream)) / 10 * 1e3
+        gm[name] = {"us": round(us, 2), "tflops": round(2.0 * n ** 3 / (us * 1e-6) / 1e12, 1)}
+    out["gemm_1024"] = gm
     return out
 
 
@@ -607,8 +697,13 @@ def run_ours(args, ctx) -> None:
     with ClockSampler(ctx["local"]) as clk:
         att = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx)
         rep = bench_attention(args.steps, args.warmup, dev, stream, ctx) if world > 1 else None
-        rows = gemm = block = None
+        rows = gemm = block = ladder = None
         if not args.headline_only:
+            if world == 1:
+                try:
+                    ladder = bench_ladder(dev, stream, pk)
+                except Exception as e:
+                    extra_err["ladder"] = repr(e)
             try:
                 rows = bench_rows(200, 5, dev, stream, pk)
             except Exception as e:  # report, keep the headline
@@ -672,12 +767,60 @@ def run_ours(args, ctx) -> None:
         line["gemm"] = gemm
     if block:
         line["decoder_block"] = block
+    if ladder:
+        line["ladder"] = ladder
     if cpu:
         line["cpu_baseline"] = cpu
         line["cpu_baseline_rows"] = cpu_rows
     if extra_err:
         line["errors"] = extra_err
     print(json.dumps(line), flush=True)
+
+
+PROFILE_CASES = ("rmsnorm", "softmax", "swiglu", "gemm1024", "gemm8192", "attention", "attention_two_tile")
+
+
+def run_profile_case(case: str, launches: int, rows: int = ROWS) -> None:
+    """Launch one kernel `launches` times, eagerly and without timing, on BASELINE-shaped
+    inputs, for an ncu capture (-k, -c). `rows` sets the row count of the row-kernel
+    cases: a [4096, 2048] output (16.8 MB) stays in L2 when ncu times a single launch, so
+    the write traffic shows only with more rows than L2 holds."""
+    import ctypes
+
+    from nkilab import _native as N
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    st = torch.cuda.current_stream(dev).cuda_stream
+    bf = torch.bfloat16
+    if case in ("rmsnorm", "softmax", "swiglu"):
+        x, u = (torch.randn(rows, COLS, device=dev, generator=g).to(bf) for _ in range(2))
+        w = (1 + 0.1 * torch.randn(COLS, device=dev, generator=g)).to(bf)
+        y = torch.empty_like(x)
+        for _ in range(launches):
+            if case == "rmsnorm":
+                N.call("nkl_rmsnorm", x.data_ptr(), w.data_ptr(), y.data_ptr(), rows, COLS, 1e-6, N.BFLOAT16, st)
+            elif case == "softmax":
+                N.call("nkl_softmax", x.data_ptr(), y.data_ptr(), rows, COLS, N.BFLOAT16, st)
+            else:
+                N.call("nkl_swiglu", x.data_ptr(), u.data_ptr(), y.data_ptr(), rows, COLS, N.BFLOAT16, st)
+    elif case.startswith("gemm"):
+        n = int(case[4:])
+        a, b = ((torch.rand(n, n, device=dev, generator=g) * 2 - 1).to(bf) for _ in range(2))
+        c = torch.empty(n, n, device=dev, dtype=bf)
+        for _ in range(launches):
+            N.call("nkl_matmul", a.data_ptr(), b.data_ptr(), c.data_ptr(), n, n, n, N.BFLOAT16, st)
+    else:
+        q, k, v = (torch.randn(H, S, D, device=dev, generator=g).to(bf) for _ in range(3))
+        o = torch.empty_like(q)
+        mode = N.ATTN_TWO_TILE if case == "attention_two_tile" else N.ATTN_AUTO
+        nbytes = N.lib.nkl_attention_mode_workspace_size(H, S, D, N.BFLOAT16, mode)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
+        for _ in range(launches):
+            N.call("nkl_attention_mode", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), ws.data_ptr(), nbytes,
+                   H, S, D, 1.0 / math.sqrt(D), N.BFLOAT16, mode, st)
+    torch.cuda.synchronize()
+    N.check_device(st)
 
 
 def main() -> None:
@@ -688,7 +831,15 @@ def main() -> None:
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--headline-only", action="store_true", help="only the attention headline (for profiling)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--profile", choices=PROFILE_CASES,
+                    help="only launch this kernel --steps times (untimed), for an ncu capture")
+    ap.add_argument("--rows", type=int, default=ROWS, help="row count of the --profile row-kernel cases")
     args = ap.parse_args()
+    if args.profile:
+        from nkilab import ops  # noqa: F401  (loads the library)
+
+        run_profile_case(args.profile, args.steps, args.rows)
+        return
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
