@@ -219,15 +219,18 @@ def bench_attention(steps: int, warmup: int, dev, stream, dist_ctx) -> dict:
             "launches_per_step": 2 if split else 1}
 
 
-def bench_attention_sharded(steps: int, warmup: int, dev, stream, ctx) -> dict:
+def bench_attention_sharded(steps: int, warmup: int, dev, stream, ctx, gather: str = "nvlink") -> dict:
     """Head-sharded attention on the fixed 8x2048x128 problem (strong scaling): rank r
-    computes heads shard_range(8, N, r) and one NCCL all-gather assembles the full
-    [8, 2048, 128] output on every rank, both inside the timed CUDA graph. The same
-    steps without the all-gather are timed separately to split out the collective."""
+    computes heads shard_range(8, N, r) and the full [8, 2048, 128] output is assembled on
+    every rank inside the timed CUDA graph -- by the attention kernels themselves over
+    NVLink (gather="nvlink", parallel.PeerAttention: output tiles stored into every rank's
+    buffer, then a flag exchange) or by an NCCL all-gather after them (gather="nccl"). The
+    same steps without any gather are timed separately to split out the collective."""
     from nkilab import _native
     from nkilab import parallel as P
 
     world, rank = ctx["world"], ctx["rank"]
+    peer = P.PeerAttention(H, S, D, device=dev) if (gather == "nvlink" and world > 1) else None
     h0, h1 = P.shard_range(H, world, rank)
     hl = h1 - h0
     per_set = 3 * hl * S * D * 2
@@ -240,8 +243,11 @@ def bench_attention_sharded(steps: int, warmup: int, dev, stream, ctx) -> dict:
 
     def step(i, gather=True):
         q, k, v = pool[i % nset]
-        local = torch.ops.nkilab.attention(q, k, v, scale, False)
-        keep.append(P.all_gather_dim0(local, H) if gather else local)
+        if gather and peer is not None:
+            keep.append(peer(q, k, v))
+        else:
+            local = torch.ops.nkilab.attention(q, k, v, scale, False)
+            keep.append(P.all_gather_dim0(local, H) if gather else local)
         if len(keep) > 2 * steps + 8:
             keep.pop(0)
 
@@ -257,9 +263,15 @@ def bench_attention_sharded(steps: int, warmup: int, dev, stream, ctx) -> dict:
     ctx["barrier"]()
     ms_compute = ctx["max"](timed_graph(lambda i: step(i, gather=False), steps, stream))
     keep.clear()
+    if peer is not None:
+        torch.cuda.synchronize()
+        _native.check_device(stream.cuda_stream)  # the flag exchange never timed out
+        peer.close()
     split = _native.lib.nkl_attention_workspace_size(hl, S, D, _native.BFLOAT16) > 0
     return {"ms_total": ms, "ms_per_step": ms / steps, "pool_sets": nset, "pool_mib": nset * per_set / 2**20,
-            "launches_per_step": 2 if split else 1, "heads_per_rank": hl, "us_per_step_rank0": spread(runs, steps),
+            "gather": gather if world > 1 else "none",
+            "launches_per_step": (2 if split else 1) + (1 if peer is not None else 0), "heads_per_rank": hl,
+            "us_per_step_rank0": spread(runs, steps),
             "attention_us": round(ms_compute / steps * 1e3, 3),
             "all_gather_us": round((ms - ms_compute) / steps * 1e3, 3) if world > 1 else 0.0}
 
@@ -273,10 +285,17 @@ def sharded_parity(dev, ctx) -> dict:
     g = torch.Generator(device=dev).manual_seed(77)
     q, k, v = (torch.randn(H, S, D, device=dev, generator=g).to(torch.bfloat16) for _ in range(3))
     got = P.attention(q, k, v)
+    peer = P.PeerAttention(H, S, D, device=dev)
+    h0, h1 = P.shard_range(H, ctx["world"], ctx["rank"])
+    got_p2p = peer(*(t[h0:h1].contiguous() for t in (q, k, v))).clone()
+    torch.cuda.synchronize()
+    peer.close()
     out = {}
     if ctx["rank"] == 0:
         ref = ops.attention(q, k, v)
         out["attn_rel_err"] = _rel(got, ref)
+        out["attn_nvlink_gather_rel_err"] = _rel(got_p2p, ref)
+        out["nvlink_gather_equals_nccl_gather"] = bool(torch.equal(got_p2p, got))
     return out
 
 
@@ -696,6 +715,7 @@ def run_ours(args, ctx) -> None:
     parity = sharded_parity(dev, ctx) if world > 1 else None
     with ClockSampler(ctx["local"]) as clk:
         att = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx)
+        att_nccl = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx, gather="nccl") if world > 1 else None
         rep = bench_attention(args.steps, args.warmup, dev, stream, ctx) if world > 1 else None
         rows = gemm = block = ladder = None
         if not args.headline_only:
@@ -735,8 +755,8 @@ def run_ours(args, ctx) -> None:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "config": {"workload": "causal attention 8x2048x128 bf16, scale 1/sqrt(128) (BASELINE configs[3])",
                    "heads": H, "seq_len": S, "head_dim": D, "batch": 1,
-                   "parallelism": (f"heads sharded over {world} GPUs ({att['heads_per_rank']} per rank) + NCCL "
-                                   "all-gather of the output to every rank, both in the timed region")
+                   "parallelism": (f"heads sharded over {world} GPUs ({att['heads_per_rank']} per rank); the output "
+                                   "gathered to every rank over NVLink by the attention kernels, in the timed region")
                    if world > 1 else "single",
                    "l2": f"rotating pool of {att['pool_sets']} input sets, {att['pool_mib']:.0f} MiB > 2x L2",
                    "launch": "K steps in one CUDA graph via torch.ops.nkilab.attention (+ all-gather)"},
@@ -746,16 +766,20 @@ def run_ours(args, ctx) -> None:
                      "algorithmic_flop_per_launch": ATTN_FLOP / world, "peak_source": pk["source"] + " burst bf16",
                      "kernel": "attn_fwd_bf16_kernel<128>",
                      "timed_over": "the whole op per step (attention kernel + split-KV combine kernel"
-                                   + (" + all-gather" if world > 1 else "") + "), per GPU, so 'achieved' is a lower "
-                                   "bound for the attention kernel alone"},
+                                   + (" + the NVLink gather and flag exchange" if world > 1 else "")
+                                   + "), per GPU, so 'achieved' is a lower bound for the attention kernel alone"},
         "clocks": clocks,
         "e2e": e2e,
         "gpu_launches": args.steps * att["launches_per_step"],
         "step_us_spread": att["us_per_step_rank0"],
     }
     if world > 1:
-        line["sharded"] = {"attention_us": att["attention_us"], "all_gather_us": att["all_gather_us"],
-                           "heads_per_rank": att["heads_per_rank"], "parity": parity}
+        line["sharded"] = {"gather": "attention kernels store every output tile into every rank's buffer over NVLink "
+                                     "(parallel.PeerAttention), then a flag exchange",
+                           "attention_us": att["attention_us"], "gather_us": att["all_gather_us"],
+                           "heads_per_rank": att["heads_per_rank"], "parity": parity,
+                           "nccl_all_gather_instead": {"us_per_step": round(att_nccl["ms_per_step"] * 1e3, 3),
+                                                       "all_gather_us": att_nccl["all_gather_us"]}}
         rms = rep["ms_per_step"]
         line["replicas"] = {"value": round(ATTN_FLOP * world / (rms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
                             "ms_per_step": round(rms, 5), "scaling": "weak",

@@ -272,6 +272,42 @@ int nkl_attention_naive(const void* q, const void* k, const void* v, void* out,
                         void* workspace, size_t workspace_bytes, int64_t heads, int64_t seq,
                         int64_t head_dim, float scale, int dtype, void* stream);
 
+/* ---- head-sharded attention with its all-gather over NVLink ----------------------- */
+
+/* Device memory several processes of one node map (CUDA IPC), for the all-gather below:
+ * nkl_ipc_alloc allocates `bytes` (zeroed) on the current device and writes its
+ * nkl_ipc_handle_bytes()-byte handle; another process opens the handle with nkl_ipc_open
+ * (a pointer valid on its current device, peer access enabled) and releases it with
+ * nkl_ipc_close; the owner frees it with nkl_ipc_free once no process uses it.
+ * No reference counterpart (the reference runs on one NeuronCore). */
+size_t nkl_ipc_handle_bytes(void);
+int nkl_ipc_alloc(size_t bytes, void** ptr, void* handle);
+int nkl_ipc_open(const void* handle, void** ptr);
+int nkl_ipc_close(void* ptr);
+int nkl_ipc_free(void* ptr);
+
+/* Causal attention of this GPU's heads, gathered into every GPU's output in the same call:
+ * q, k, v [heads, seq, head_dim] bf16 are this rank's heads, which are heads
+ * [head_offset, head_offset + heads) of the full [heads_total, seq, head_dim] output.
+ * outs[r] is rank r's output buffer and flags[r] rank r's flag array (world + 1 uint32,
+ * zeroed before the first call), as pointers valid on this device (nkl_ipc_open for the
+ * other ranks'). The attention kernel stores each finished output tile into every rank's
+ * buffer over NVLink (TMA stores; split tiles' merge kernel writes every buffer too), then a
+ * one-warp kernel exchanges per-call counts through the flag arrays (system-scope release /
+ * acquire, bounded wait: NKL_ERR_DEVICE from nkl_check_device if a peer never arrives), so
+ * when the call's work on `stream` completes, every rank's heads are in this rank's buffer.
+ * Every rank must make the same sequence of calls. A rank writes into the others' buffers
+ * while they may still read the previous call's result, so alternate two buffer sets
+ * between consecutive calls (the second-previous call's readers on every rank have finished
+ * when the previous call's count exchange completes). workspace as nkl_attention_ws for
+ * (heads, seq, head_dim). world <= 8, bf16, head_dim 64 or 128.
+ * Replaces nkilab/ops.py:77-91 (attention) for the head sharding and output gather the
+ * B200 build adds; the reference has no distributed code. */
+int nkl_attention_allgather(const void* q, const void* k, const void* v, void* const* outs,
+                            unsigned int* const* flags, int world, int rank, int64_t heads_total,
+                            int64_t head_offset, void* workspace, size_t workspace_bytes, int64_t heads,
+                            int64_t seq, int64_t head_dim, float scale, int dtype, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -173,6 +173,16 @@ struct AttnArgs {
   uint2 unit_desc[kMaxSched];
 };
 
+// Extra output destinations for the head-sharded all-gather (nkl_attention_allgather): the
+// other GPUs' output buffers, written through NVLink by the same epilogue that writes this
+// GPU's, at head index local head + head_offset (also in this GPU's buffer).
+constexpr int kMaxPeers = 7;
+struct PeerOut {
+  CUtensorMap map[kMaxPeers];  // peers' [heads_total, seq, d] outputs, same layout as map_o
+  int n;                       // peer destinations (0: none)
+  int head_offset;
+};
+
 struct Unit {
   int head, qt, chunk, n_chunks, j0, n, v0;  // v0: per-head index of this query tile's chunk 0
 };
@@ -261,7 +271,7 @@ template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
-                     const __grid_constant__ AttnArgs args) {
+                     const __grid_constant__ AttnArgs args, const __grid_constant__ PeerOut peers) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   if (smem_u32(smem_raw) & 1023u) {  // the swizzled tiles need a 1024-byte-aligned base
     if (threadIdx.x == 0) atomicCAS(&g_attn_dev_error, 0u, 40u);
@@ -487,6 +497,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     const int pair_id = 1 + qd;
     const int sw = r & 7;
     const bool quad_lead = hf == 0 && lane == 0;  // stores its quadrant's output rows, frees the Q buffer
+    bool stored_any = false;
     uint32_t gt = 0, uc = 0;
     bool ok = true;
     UnitRun un;
@@ -599,11 +610,17 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         pair_sync(pair_id);
         const int row0 = qt * kTile + qd * 32;
         if (quad_lead && row0 < args.seq) {
+          const int oh = un.head + peers.head_offset;
 #pragma unroll
           for (int c = 0; c < kSub; ++c)
-            tma_store_3d(&map_o, s.q[qb] + c * (kTile * 128) + qd * 32 * 128, c * 64, row0, un.head);
+            tma_store_3d(&map_o, s.q[qb] + c * (kTile * 128) + qd * 32 * 128, c * 64, row0, oh);
+          for (int p = 0; p < peers.n; ++p)  // the same staged rows into every peer's buffer
+#pragma unroll
+            for (int c = 0; c < kSub; ++c)
+              tma_store_3d(&peers.map[p], s.q[qb] + c * (kTile * 128) + qd * 32 * 128, c * 64, row0, oh);
           tma_store_commit();
           tma_store_wait_read();
+          stored_any = true;
         }
       }
       // the Q buffer may be refilled once every quadrant's output staging has been read
@@ -611,6 +628,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       gt += (uint32_t)un.n;
       ++uc;
     }
+    // every output store, local and remote, has completed before the CTA exits
+    if (stored_any) tma_store_wait_all();
   }
 
   tc_fence_before();
@@ -639,6 +658,8 @@ struct CombineJob {
 struct CombineArgs {
   const unsigned char* ws;
   bf16* out;
+  bf16* peer_out[kMaxPeers];  // the all-gather's peer destinations (n_peer of them)
+  int n_peer, head_offset;    // output head = head + head_offset in every destination
   int heads, seq, n_jobs;
   size_t ws_stats_off, ws_o_off;
   int64_t o_ss, o_hs;  // output strides in elements: between rows (seq) and between heads
@@ -686,7 +707,8 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     lsum += wc[c];
   }
   const float inv = 1.0f / lsum;
-  uint4* dst = reinterpret_cast<uint4*>(args.out + (size_t)head * args.o_hs + (size_t)row * args.o_ss + g0 * 8);
+  const size_t o_off = (size_t)(head + args.head_offset) * args.o_hs + (size_t)row * args.o_ss + g0 * 8;
+  uint4* dst = reinterpret_cast<uint4*>(args.out + o_off);
 #pragma unroll
   for (int g = 0; g < GPT; ++g) {
     float f[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -702,7 +724,9 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
     }
 #pragma unroll
     for (int k2 = 0; k2 < 8; ++k2) f[k2] *= inv;
-    dst[g] = pack16<bf16>(f);
+    const uint4 packed = pack16<bf16>(f);
+    dst[g] = packed;
+    for (int p = 0; p < args.n_peer; ++p) reinterpret_cast<uint4*>(args.peer_out[p] + o_off)[g] = packed;
   }
 }
 
@@ -1027,14 +1051,28 @@ const AttnPlan& cached_plan(int heads, int kv_group, int seq, int d, bool allow_
   return it->second;
 }
 
+// The all-gather's other destinations, for launch_attn_bf16: peer output buffers of
+// [heads_total, seq, d] (contiguous) and the head offset of this GPU's heads in them.
+struct PeerDest {
+  bf16* out[kMaxPeers];
+  int n = 0, heads_total = 0, head_offset = 0;
+};
+
 template <int D>
 int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int heads, int kv_heads, int seq,
-                     float scale, void* ws, size_t ws_bytes, const AttnLayout& lay, cudaStream_t st) {
+                     float scale, void* ws, size_t ws_bytes, const AttnLayout& lay, cudaStream_t st,
+                     const PeerDest* pd = nullptr) {
   CUtensorMap mq, mk, mv, mo;
+  PeerOut peers;
+  peers.n = pd ? pd->n : 0;
+  peers.head_offset = pd ? pd->head_offset : 0;
+  const int out_heads = pd ? pd->heads_total : heads;
   int rc = make_qkv_map(&mq, q, heads, seq, D, lay.q_ss, lay.q_hs, "nkl_attention(q)");
   if (!rc) rc = make_qkv_map(&mk, k, kv_heads, seq, D, lay.k_ss, lay.k_hs, "nkl_attention(k)");
   if (!rc) rc = make_qkv_map(&mv, v, kv_heads, seq, D, lay.v_ss, lay.v_hs, "nkl_attention(v)");
-  if (!rc) rc = make_qkv_map(&mo, out, heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)", 32);
+  if (!rc) rc = make_qkv_map(&mo, out, out_heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(out)", 32);
+  for (int p = 0; !rc && p < peers.n; ++p)
+    rc = make_qkv_map(&peers.map[p], pd->out[p], out_heads, seq, D, lay.o_ss, lay.o_hs, "nkl_attention(peer out)", 32);
   if (rc) return rc;
   const AttnPlan& plan = cached_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
@@ -1063,7 +1101,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
   for (size_t i = 0; i < plan.unit_desc.size(); ++i) a.unit_desc[i] = plan.unit_desc[i];
   rc = launch_pdl(attn_fwd_bf16_kernel<D>, dim3(plan.ctas), dim3(kAttnThreads), smem, st, "nkl_attention", mq, mk, mv,
-                  mo, a);
+                  mo, a, peers);
   if (rc || plan.jobs.empty()) return rc;
   // split query tiles: merge the partials (programmatic dependent launch: the combine
   // grid is scheduled early and waits on the device for the attention grid)
@@ -1072,6 +1110,9 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   std::lock_guard<std::mutex> lock(ca_mu);
   ca.ws = static_cast<const unsigned char*>(ws);
   ca.out = static_cast<bf16*>(out);
+  ca.n_peer = peers.n;
+  ca.head_offset = peers.head_offset;
+  for (int p = 0; p < peers.n; ++p) ca.peer_out[p] = pd->out[p];
   ca.heads = heads;
   ca.seq = seq;
   ca.n_jobs = (int)plan.jobs.size();
@@ -1279,6 +1320,8 @@ int launch_attn_pair_bf16(const void* q, const void* k, const void* v, void* out
   static CombineArgs ca;
   ca.ws = static_cast<const unsigned char*>(ws);
   ca.out = static_cast<bf16*>(out);
+  ca.n_peer = 0;
+  ca.head_offset = 0;
   ca.heads = heads;
   ca.seq = seq;
   ca.n_jobs = (int)plan.jobs.size();
@@ -1293,6 +1336,50 @@ int launch_attn_pair_bf16(const void* q, const void* k, const void* v, void* out
   if (plan.max_chunks <= 4)
     return launch_pdl(attn_combine_bf16_kernel<D, 4>, grid(4), dim3(64), 0, st, "nkl_attention(combine)", ca);
   return launch_pdl(attn_combine_bf16_kernel<D, 8>, grid(8), dim3(64), 0, st, "nkl_attention(combine)", ca);
+}
+
+// ---- the all-gather's completion barrier over NVLink
+// Every rank's flag array holds world + 1 words in device memory that all ranks map (CUDA
+// IPC): word j is written by rank j when it has finished writing its heads into every
+// buffer, word `world` is the owner's call count. One warp: rank r stores its new count
+// into word r of every peer's array (release, system scope, after a system-scope fence),
+// then waits until every peer's word in its own array has reached the count (acquire,
+// bounded: after kWaitTimeoutNs it records code 90 in the device flag and returns). The
+// counts only grow, so a peer that is already one call ahead satisfies the wait too.
+struct PeerFlags {
+  unsigned int* ptr[kMaxPeers + 1];  // indexed by rank
+  int world, rank;
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned int* p, unsigned int v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
+  unsigned int v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(32) peer_barrier_kernel(const __grid_constant__ PeerFlags f) {
+  const int t = threadIdx.x;
+  unsigned int* mine = f.ptr[f.rank];
+  unsigned int epoch = 0;
+  if (t == 0) epoch = mine[f.world] + 1u;
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
+  asm volatile("fence.sc.sys;" ::: "memory");  // this GPU's output writes (earlier kernels) before the flags
+  const bool peer = t < f.world && t != f.rank;
+  if (peer) st_release_sys(f.ptr[t] + f.rank, epoch);
+  if (peer) {
+    const uint64_t t0 = globaltimer();
+    while ((int)(ld_acquire_sys(mine + t) - epoch) < 0) {
+      if (globaltimer() - t0 > kWaitTimeoutNs) {
+        atomicCAS(&g_attn_dev_error, 0u, 90u);
+        break;
+      }
+    }
+  }
+  __syncwarp();
+  if (t == 0) mine[f.world] = epoch;
 }
 
 int check_attn(const char* op, int64_t heads, int64_t seq, int64_t d, int dtype) {
@@ -1325,7 +1412,7 @@ namespace {
 int attention_impl(const char* op, const void* q, const void* k, const void* v, void* out, void* workspace,
                    size_t workspace_bytes, int64_t heads, int64_t kv_heads, int64_t seq, int64_t head_dim,
                    float scale, int dtype, void* stream, const AttnLayout* layout = nullptr,
-                   int mode = NKL_ATTN_AUTO) {
+                   int mode = NKL_ATTN_AUTO, const PeerDest* peers = nullptr) {
   int rc = check_attn(op, heads, seq, head_dim, dtype);
   if (rc) return rc;
   if (heads == 0 || seq == 0) return NKL_OK;
@@ -1360,9 +1447,9 @@ int attention_impl(const char* op, const void* q, const void* k, const void* v, 
   if (mode == NKL_ATTN_ONE_TILE_UNSPLIT) workspace = nullptr;
   if (head_dim == 64)
     return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                                workspace ? workspace_bytes : 0, lay, st);
+                                workspace ? workspace_bytes : 0, lay, st, peers);
   return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                               workspace ? workspace_bytes : 0, lay, st);
+                               workspace ? workspace_bytes : 0, lay, st, peers);
 }
 
 }  // namespace
@@ -1472,4 +1559,37 @@ extern "C" int nkl_attention_mode(const void* q, const void* k, const void* v, v
     return fail(NKL_ERR_DTYPE, "nkl_attention_mode: the two-query-tile kernel is bf16 only");
   return attention_impl("nkl_attention_mode", q, k, v, out, dtype == NKL_BFLOAT16 ? workspace : nullptr,
                         workspace_bytes, heads, heads, seq, head_dim, scale, dtype, stream, nullptr, mode);
+}
+
+extern "C" int nkl_attention_allgather(const void* q, const void* k, const void* v, void* const* outs,
+                                       unsigned int* const* flags, int world, int rank, int64_t heads_total,
+                                       int64_t head_offset, void* workspace, size_t workspace_bytes, int64_t heads,
+                                       int64_t seq, int64_t head_dim, float scale, int dtype, void* stream) {
+  const char* op = "nkl_attention_allgather";
+  if (dtype != NKL_BFLOAT16) return fail(NKL_ERR_DTYPE, "%s: bf16 only", op);
+  if (world < 1 || world > kMaxPeers + 1 || rank < 0 || rank >= world)
+    return fail(NKL_ERR_ARG, "%s: need 1 <= world <= %d and 0 <= rank < world (got %d, %d)", op, kMaxPeers + 1, world,
+                rank);
+  if (heads < 1 || head_offset < 0 || heads_total < heads || head_offset > heads_total - heads || heads_total > 65535)
+    return fail(NKL_ERR_SHAPE, "%s: heads [%lld, %lld) outside the %lld output heads", op, (long long)head_offset,
+                (long long)(head_offset + heads), (long long)heads_total);
+  if (!outs || !flags) return fail(NKL_ERR_ARG, "%s: NULL pointer array", op);
+  PeerDest pd;
+  pd.heads_total = (int)heads_total;
+  pd.head_offset = (int)head_offset;
+  PeerFlags pf;
+  pf.world = world;
+  pf.rank = rank;
+  for (int r = 0; r < world; ++r) {
+    if (!outs[r] || !flags[r]) return fail(NKL_ERR_ARG, "%s: NULL buffer of rank %d", op, r);
+    if (!is_aligned(outs[r], 16) || !is_aligned(flags[r], 16))
+      return fail(NKL_ERR_ALIGN, "%s: buffers must be 16-byte aligned (rank %d)", op, r);
+    pf.ptr[r] = flags[r];
+    if (r != rank) pd.out[pd.n++] = static_cast<bf16*>(outs[r]);
+  }
+  int rc = attention_impl(op, q, k, v, outs[rank], workspace, workspace_bytes, heads, heads, seq, head_dim, scale,
+                          dtype, stream, nullptr, NKL_ATTN_AUTO, &pd);
+  if (rc || world == 1) return rc;
+  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pf);
+  return check_launch(op);
 }

@@ -3,6 +3,8 @@
 // kernels (rows.cu, gemm.cu, attention.cu).
 #include <atomic>
 
+#include <cstring>
+
 #include "common.cuh"
 
 namespace nkl {
@@ -52,4 +54,41 @@ extern "C" int nkl_check_device(void* stream) {
   if (g || a)
     return nkl::fail(NKL_ERR_DEVICE, "nkl_check_device: kernel gave up waiting (gemm code %d, attention code %d)", g, a);
   return NKL_OK;
+}
+
+// ---- device memory shared between the processes of one node (CUDA IPC), for the
+// all-gather's output buffers and flag arrays
+
+extern "C" size_t nkl_ipc_handle_bytes(void) { return sizeof(cudaIpcMemHandle_t); }
+
+extern "C" int nkl_ipc_alloc(size_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return nkl::fail(NKL_ERR_ARG, "nkl_ipc_alloc: bad argument");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, bytes);
+  if (e == cudaSuccess) e = cudaMemset(p, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(static_cast<cudaIpcMemHandle_t*>(handle), p);
+  if (e != cudaSuccess) {
+    if (p) cudaFree(p);
+    return nkl::fail(NKL_ERR_CUDA, "nkl_ipc_alloc: %s", cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return NKL_OK;
+}
+
+extern "C" int nkl_ipc_open(const void* handle, void** ptr) {
+  if (!ptr || !handle) return nkl::fail(NKL_ERR_ARG, "nkl_ipc_open: NULL argument");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  return e == cudaSuccess ? NKL_OK : nkl::fail(NKL_ERR_CUDA, "nkl_ipc_open: %s", cudaGetErrorString(e));
+}
+
+extern "C" int nkl_ipc_close(void* ptr) {
+  cudaError_t e = cudaIpcCloseMemHandle(ptr);
+  return e == cudaSuccess ? NKL_OK : nkl::fail(NKL_ERR_CUDA, "nkl_ipc_close: %s", cudaGetErrorString(e));
+}
+
+extern "C" int nkl_ipc_free(void* ptr) {
+  cudaError_t e = cudaFree(ptr);
+  return e == cudaSuccess ? NKL_OK : nkl::fail(NKL_ERR_CUDA, "nkl_ipc_free: %s", cudaGetErrorString(e));
 }

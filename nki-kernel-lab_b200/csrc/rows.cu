@@ -68,19 +68,31 @@ rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restr
                     float inv_cols, float eps) {
   constexpr int V = Vec16<T>::N;
   pdl_launch_dependents();
+  // The weight row, staged once per block: every warp reads it right after its reduction,
+  // from shared memory instead of an L2 round trip on its critical path.
+  __shared__ uint4 wsm[NV * 32];
   const int64_t row = (int64_t)blockIdx.x * kRmsWarpsPerBlock + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row < rows && lane == 0) l2_prefetch(x + row * cols, (uint32_t)(cols * sizeof(T)));
   pdl_wait();
-  if (row >= rows) return;
   const int nvec = cols / V;
   const T* xr = x + row * cols;
   Vec16<T> xv[NV];
+  if (row < rows) {  // the row's loads go out first; the weight loads overlap their latency
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const int j = i * 32 + lane;
-    xv[i].raw = (FULL || j < nvec) ? ld_stream(xr + j * V) : make_uint4(0u, 0u, 0u, 0u);
+    for (int i = 0; i < NV; ++i) {
+      const int j = i * 32 + lane;
+      xv[i].raw = (FULL || j < nvec) ? ld_stream(xr + j * V) : make_uint4(0u, 0u, 0u, 0u);
+    }
   }
+  constexpr int kPerThread = (NV * 32 + kRmsWarpsPerBlock * 32 - 1) / (kRmsWarpsPerBlock * 32);
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int j = k * kRmsWarpsPerBlock * 32 + (int)threadIdx.x;
+    if (j < nvec) wsm[j] = *reinterpret_cast<const uint4*>(w + j * V);
+  }
+  __syncthreads();
+  if (row >= rows) return;
   // Four partial sums break the dependent chain of NV * V fused multiply-adds.
   float ssq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -96,7 +108,7 @@ rmsnorm_warp_kernel(const T* __restrict__ x, const T* __restrict__ w, T* __restr
     const int j = i * 32 + lane;
     if (FULL || j < nvec) {
       Vec16<T> wv;
-      wv.raw = *reinterpret_cast<const uint4*>(w + j * V + z);
+      wv.raw = wsm[j + z];
       float o[V];
 #pragma unroll
       for (int e = 0; e < V; ++e) o[e] = (vec_get_tied(xv[i], e, z) * rstd) * wv.get(e);  // fp32 x * rstd, then * weight

@@ -63,6 +63,13 @@ SIGNATURES = {
     "nkl_attention_gqa": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _i64, _f, _int, _p]),
     "nkl_attention_mode_workspace_size": (_sz, [_i64, _i64, _i64, _int, _int]),
     "nkl_attention_mode": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _int, _p]),
+    "nkl_ipc_handle_bytes": (_sz, []),
+    "nkl_ipc_alloc": (_int, [_sz, _p, _p]),
+    "nkl_ipc_open": (_int, [_p, _p]),
+    "nkl_ipc_close": (_int, [_p]),
+    "nkl_ipc_free": (_int, [_p]),
+    "nkl_attention_allgather": (_int, [_p, _p, _p, _p, _p, _int, _int, _i64, _i64, _p, _sz, _i64, _i64, _i64, _f, _int,
+                                       _p]),
     "nkl_attention_naive_workspace_size": (_sz, [_i64, _i64, _int]),
     "nkl_attention_naive": (_int, [_p, _p, _p, _p, _p, _sz, _i64, _i64, _i64, _f, _int, _p]),
 }

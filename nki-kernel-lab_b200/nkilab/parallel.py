@@ -24,6 +24,7 @@ so the host-side logic can be exercised with gloo ranks on CPU in tests.
 """
 from __future__ import annotations
 
+import ctypes
 import math
 from dataclasses import dataclass
 from typing import Callable, Optional, Sequence
@@ -120,6 +121,116 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, variant: str = 
     fn = compute or _default_attention
     local = fn(q[h0:h1].contiguous(), k[h0:h1].contiguous(), v[h0:h1].contiguous(), variant)
     return all_gather_dim0(local, H, group)
+
+
+class _RawCuda:
+    """A device allocation seen through __cuda_array_interface__, so torch.as_tensor can
+    view it without a copy (as uint16; the caller views it as bfloat16)."""
+
+    def __init__(self, ptr: int, shape: tuple):
+        self.__cuda_array_interface__ = {"shape": shape, "typestr": "<u2", "data": (ptr, False), "version": 3,
+                                         "strides": None}
+
+
+class PeerAttention:
+    """Head-sharded causal attention whose output gather runs over NVLink inside the
+    attention launch (nkl_attention_allgather): every rank's attention kernel stores its
+    finished output tiles into every rank's output buffer (CUDA IPC mappings of one
+    buffer per rank), then a one-warp kernel exchanges per-call counts, so no library
+    collective is involved. This is the B200 form of parallel.attention's
+    compute-then-all-gather (which uses NCCL).
+
+    Buffers: two output sets of [heads_total, seq, head_dim] bf16 per rank (consecutive
+    calls alternate, so a rank never writes into a buffer a peer may still be reading) and
+    one flag array, allocated once, their IPC handles exchanged with all_gather_object.
+    __call__(q, k, v) takes this rank's heads (shard_range(heads_total, world, rank)) as
+    contiguous bf16 CUDA tensors [local_heads, seq, head_dim] and returns this rank's full
+    output buffer; it stays valid until the call after next (copy it to keep it longer).
+    Every rank must make the same calls in the same order. close() (collective) releases
+    the buffers."""
+
+    def __init__(self, heads_total: int, seq: int, head_dim: int, group=None, device=None):
+        from . import _native as N
+
+        self.world, self.rank = _world(group)
+        self.group = group
+        self.heads_total, self.seq, self.head_dim = heads_total, seq, head_dim
+        self.h0, self.h1 = shard_range(heads_total, self.world, self.rank)
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+        hb = int(N.lib.nkl_ipc_handle_bytes())
+        self._own, self._opened = [], []
+        nbytes = heads_total * seq * head_dim * 2
+        handles = []
+        with torch.cuda.device(self.device):
+            for size in (nbytes, nbytes, 256):  # output set 0, output set 1, flags (world + 1 words)
+                ptr, h = ctypes.c_void_p(), ctypes.create_string_buffer(hb)
+                N.call("nkl_ipc_alloc", size, ctypes.byref(ptr), h)
+                self._own.append(ptr.value)
+                handles.append(h.raw)
+            if self.world > 1:
+                every = [None] * self.world
+                dist.all_gather_object(every, handles, group=group)
+            else:
+                every = [handles]
+            ptrs = []  # ptrs[r] = (out0, out1, flags) of rank r, valid on this device
+            for r in range(self.world):
+                if r == self.rank:
+                    ptrs.append(tuple(self._own))
+                    continue
+                opened = []
+                for h in every[r]:
+                    p = ctypes.c_void_p()
+                    N.call("nkl_ipc_open", ctypes.create_string_buffer(h, hb), ctypes.byref(p))
+                    opened.append(p.value)
+                    self._opened.append(p.value)
+                ptrs.append(tuple(opened))
+        arr = ctypes.c_void_p * self.world
+        self._outs = [arr(*[ptrs[r][i] for r in range(self.world)]) for i in (0, 1)]
+        self._flags = arr(*[ptrs[r][2] for r in range(self.world)])
+        shape = (heads_total, seq, head_dim)
+        self._views = [torch.as_tensor(_RawCuda(self._own[i], shape), device=self.device).view(torch.bfloat16)
+                       for i in (0, 1)]
+        self._calls = 0
+        self.scale = 1.0 / math.sqrt(head_dim)
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        from . import _native as N
+        from . import _torch_ops
+
+        hl = self.h1 - self.h0
+        want = (hl, self.seq, self.head_dim)
+        for t in (q, k, v):
+            if t.shape != want or t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"PeerAttention: q, k, v must be contiguous bf16 {want} on {self.device}")
+        which = self._calls & 1
+        self._calls += 1
+        st = torch.cuda.current_stream(self.device).cuda_stream
+        with torch.cuda.device(self.device):
+            nbytes = N.lib.nkl_attention_workspace_size(hl, self.seq, self.head_dim, N.BFLOAT16)
+            ws = _torch_ops._attention_workspace(self.device, st, nbytes) if nbytes else None
+            N.call("nkl_attention_allgather", q.data_ptr(), k.data_ptr(), v.data_ptr(), self._outs[which], self._flags,
+                   self.world, self.rank, self.heads_total, self.h0, ws.data_ptr() if ws is not None else None, nbytes,
+                   hl, self.seq, self.head_dim, self.scale, N.BFLOAT16, st)
+        return self._views[which]
+
+    def close(self) -> None:
+        """Collective: every rank waits for the others, then releases its mappings and frees
+        its buffers."""
+        from . import _native as N
+
+        if not self._own:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for p in self._opened:
+                N.call("nkl_ipc_close", ctypes.c_void_p(p))
+            if self.world > 1:
+                dist.barrier(group=self.group)
+            for p in self._own:
+                N.call("nkl_ipc_free", ctypes.c_void_p(p))
+        self._own, self._opened, self._views = [], [], []
 
 
 def row_op(op: str, *tensors: torch.Tensor, group=None, compute: Optional[Callable] = None, **kw) -> torch.Tensor:

@@ -48,6 +48,23 @@ def _worker(rank: int, world: int, port: int) -> None:
         assert got.shape == ref.shape
         assert rel_err(got.float().cpu().numpy(), ref.float().cpu().numpy()) < 3e-3
 
+        # the same head sharding with the gather done by the attention kernels over NVLink
+        # (PeerAttention): the same kernels on the same local heads, so the same bits as the
+        # NCCL-gathered output, on three calls in a row (both buffer sets, then the first again)
+        pa = P.PeerAttention(8, 2048, 128, device=dev)
+        try:
+            h0, h1 = P.shard_range(8, world, rank)
+            for call in range(3):
+                qc, kc, vc = (torch.randn(8, 2048, 128, generator=g).to(torch.bfloat16).to(dev) for _ in range(3))
+                ref = P.attention(qc, kc, vc)
+                got = pa(*(t[h0:h1].contiguous() for t in (qc, kc, vc)))
+                torch.cuda.synchronize()
+                ops_check = __import__("nkilab._native", fromlist=["check_device"])
+                ops_check.check_device(torch.cuda.current_stream().cuda_stream)
+                assert torch.equal(got, ref), f"call {call}"
+        finally:
+            pa.close()
+
         # row-sharded RMSNorm: the same kernel on each row -> identical rows
         x = torch.randn(4096, 2048, generator=g).to(torch.bfloat16).to(dev)
         w = (1 + 0.1 * torch.randn(2048, generator=g)).to(torch.bfloat16).to(dev)
