@@ -424,8 +424,10 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         out["parallelism"] = "single"
     else:
         w = P.shard_block(block, world, rank, torch.bfloat16, dev)
-        fwd = lambda marks=None: P.decoder_block(block, x, weights=w, marks=marks)  # noqa: E731
-        out["parallelism"] = f"tp{world} heads x ffn columns, sequence-parallel rows, fp32 reduce-scatter"
+        serial = lambda marks=None: P.decoder_block(block, x, weights=w, marks=marks)  # noqa: E731
+        fwd = lambda: P.decoder_block_overlapped(block, x, weights=w)  # noqa: E731
+        out["parallelism"] = (f"tp{world} heads x ffn columns, sequence-parallel rows, fp32 reduce-scatter; "
+                              "collectives of each batch element overlapped with the next one's GEMMs")
         with torch.cuda.stream(stream):
             y = fwd()
             torch.cuda.synchronize()
@@ -453,10 +455,21 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         t1.record(stream)
         torch.cuda.synchronize()
         ms = ctx["max"](t0.elapsed_time(t1) / steps)
-        if world > 1:  # one more step with events at the phase boundaries
+        if world > 1:  # the same block without the overlap, with events at the phase boundaries
+            ctx["barrier"]()
+            for _ in range(2):
+                serial()
+            torch.cuda.synchronize()
+            ctx["barrier"]()
+            t0.record(stream)
+            for _ in range(steps):
+                serial()
+            t1.record(stream)
+            torch.cuda.synchronize()
+            out["ms_without_overlap"] = round(ctx["max"](t0.elapsed_time(t1) / steps), 3)
             ctx["barrier"]()
             marks = []
-            fwd(marks)
+            serial(marks)
             torch.cuda.synchronize()
             names = [n for n, _ in marks]
             spans = {names[i]: marks[i - 1][1].elapsed_time(marks[i][1]) for i in range(1, len(marks))}

@@ -1361,6 +1361,10 @@ __device__ __forceinline__ unsigned int ld_acquire_sys(const unsigned int* p) {
 }
 
 __global__ void __launch_bounds__(32) peer_barrier_kernel(const __grid_constant__ PeerFlags f) {
+  // Launched with programmatic dependent launch behind the attention (or merge) kernel:
+  // scheduled early, it waits here until that grid has completed and its writes, the
+  // stores into the other GPUs' buffers included, are performed.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const int t = threadIdx.x;
   unsigned int* mine = f.ptr[f.rank];
   unsigned int epoch = 0;
@@ -1590,6 +1594,5 @@ extern "C" int nkl_attention_allgather(const void* q, const void* k, const void*
   int rc = attention_impl(op, q, k, v, outs[rank], workspace, workspace_bytes, heads, heads, seq, head_dim, scale,
                           dtype, stream, nullptr, NKL_ATTN_AUTO, &pd);
   if (rc || world == 1) return rc;
-  peer_barrier_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(pf);
-  return check_launch(op);
+  return launch_pdl(peer_barrier_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), op, pf);
 }

@@ -359,6 +359,87 @@ class _Marks:
             self.record.append((name, ev))
 
 
+def decoder_block_overlapped(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights] = None,
+                             group=None) -> torch.Tensor:
+    """decoder_block for x [B, S, d] bf16 on CUDA with the collectives overlapped with the
+    GEMMs: the batch elements go through the block one after another, each one's row
+    all-gathers and fp32 reduce-scatters issued asynchronously (NCCL's stream) while the
+    next element's projections and attention run. Rows are sharded per batch element
+    (rank r holds rows shard_range(S, world, r) of every element, S % world == 0); every
+    kernel, rounding point and fp32 reduction is that of decoder_block, row for row.
+    Falls back to decoder_block when the shape does not allow it."""
+    world, rank = _world(group)
+    B = x.shape[0] if x.dim() == 3 else 1
+    cfg = block.cfg
+    if (world == 1 or x.dim() != 3 or B < 2 or x.shape[1] % world or not x.is_cuda
+            or x.dtype != torch.bfloat16 or cfg.head_dim not in (64, 128)):
+        return decoder_block(block, x, weights=weights, group=group)
+    _, S, d = x.shape
+    hd = cfg.head_dim
+    w = weights or shard_block(block, world, rank, x.dtype, x.device)
+    nh = w.heads[1] - w.heads[0]
+    s0, s1 = shard_range(S, world, rank)
+    bf, f32 = torch.bfloat16, torch.float32
+    dev = x.device
+    x_loc = [x[b, s0:s1].contiguous() for b in range(B)]
+
+    def ag(local):  # all-gather of one element's row shards, asynchronously
+        full = torch.empty((S, d), dtype=local.dtype, device=dev)
+        return full, dist.all_gather_into_tensor(full, local, group=group, async_op=True)
+
+    def rs(part):  # fp32 reduce-scatter of one element's partial products, asynchronously
+        out = torch.empty((s1 - s0, d), dtype=f32, device=dev)
+        return out, dist.reduce_scatter_tensor(out, part, op=dist.ReduceOp.SUM, group=group, async_op=True)
+
+    # attention half
+    gathered = [ag(ops_rmsnorm(xl, w.norm1, cfg.eps)) for xl in x_loc]
+    reduced = []
+    for full, work in gathered:
+        work.wait()  # the compute stream waits for the collective, the host does not
+        if nh > 0:
+            qkv = torch.ops.nkilab.matmul(full, w.wqkv, False).view(S, 3, nh, hd)
+            a = torch.empty(S, nh, hd, dtype=bf, device=dev)
+            q, k, v = (qkv[:, i].transpose(0, 1) for i in range(3))
+            torch.ops.nkilab.attention_strided_(q, k, v, a.transpose(0, 1), 1.0 / math.sqrt(hd))
+            part = torch.ops.nkilab.matmul_f32out(a.view(S, nh * hd), w.wo)
+        else:
+            part = torch.zeros((S, d), dtype=f32, device=dev)
+        reduced.append(rs(part))
+    # MLP half
+    x1, gathered = [], []
+    for xl, (attn_out, work) in zip(x_loc, reduced):
+        work.wait()
+        xb, hb = torch.ops.nkilab.add_rmsnorm(xl, attn_out.to(bf), w.norm2, cfg.eps)
+        x1.append(xb)
+        gathered.append(ag(hb))
+    reduced = []
+    for full, work in gathered:
+        work.wait()
+        if w.ff[1] > w.ff[0]:
+            if w.wgu is not None:
+                act = torch.ops.nkilab.matmul_swiglu(full, w.wgu)
+            else:
+                act = torch.ops.nkilab.swiglu(torch.ops.nkilab.matmul(full, w.wg, False),
+                                              torch.ops.nkilab.matmul(full, w.wu, False))
+            part = torch.ops.nkilab.matmul_f32out(act, w.wd)
+        else:
+            part = torch.zeros((S, d), dtype=f32, device=dev)
+        reduced.append(rs(part))
+    out = torch.empty((B, S, d), dtype=bf, device=dev)
+    works = []
+    for b, (xb, (mlp_out, work)) in enumerate(zip(x1, reduced)):
+        work.wait()
+        yb = (xb.float() + mlp_out.to(bf).float()).to(bf)
+        works.append(dist.all_gather_into_tensor(out[b], yb, group=group, async_op=True))
+    for work in works:
+        work.wait()
+    return out
+
+
+def ops_rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    return torch.ops.nkilab.rmsnorm(x, weight, eps)
+
+
 def decoder_block(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights] = None,
                   variant: str = "flash_pipelined", group=None, ops_module=None,
                   marks: Optional[list] = None) -> torch.Tensor:

@@ -91,6 +91,10 @@ def _worker(rank: int, world: int, port: int) -> None:
         for b_i in range(2):
             o32, o64 = _oracle_pair(block, xb[b_i])
             assert_block_parity(got_b[b_i].float().cpu().numpy(), o32, o64)
+        # the same block with the collectives overlapped per batch element: the same kernels
+        # row for row and two-rank fp32 sums, so the same bits
+        got_o = P.decoder_block_overlapped(block, xb.to(dev), weights=w)
+        assert torch.equal(got_o, got_b)
         dist.barrier()
     finally:
         dist.destroy_process_group()
