@@ -455,6 +455,21 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         t1.record(stream)
         torch.cuda.synchronize()
         ms = ctx["max"](t0.elapsed_time(t1) / steps)
+        if world > 1:  # SMs left to NCCL while the overlapped block's GEMMs run
+            by_sms = {}
+            for c in (16, 32):
+                ctx["barrier"]()
+                P.decoder_block_overlapped(block, x, weights=w, comm_sms=c)
+                torch.cuda.synchronize()
+                ctx["barrier"]()
+                t0.record(stream)
+                for _ in range(steps):
+                    P.decoder_block_overlapped(block, x, weights=w, comm_sms=c)
+                t1.record(stream)
+                torch.cuda.synchronize()
+                by_sms[c] = round(ctx["max"](t0.elapsed_time(t1) / steps), 3)
+            by_sms[0] = round(ms, 3)
+            out["ms_by_comm_sms"] = {str(k): by_sms[k] for k in sorted(by_sms)}
         if world > 1:  # the same block without the overlap, with events at the phase boundaries
             ctx["barrier"]()
             for _ in range(2):

@@ -68,6 +68,14 @@ const char* nkl_last_error(void);
  * NKL_ERR_DEVICE. The reference has no device and no counterpart. */
 int nkl_check_device(void* stream);
 
+/* Number of SMs the persistent GEMM and attention kernels launched from the calling host
+ * thread may fill (their grids and work plans size to it); 0 = all SMs, the default. The
+ * tensor-parallel decoder block lowers it while its NCCL collectives run beside the GEMMs,
+ * so the collectives' kernels find free SMs; results do not depend on it except through the
+ * attention's split-KV plan. *previous (if not NULL) receives the value it replaces.
+ * No reference counterpart (library plumbing). */
+int nkl_set_sm_budget(int sms, int* previous);
+
 /* ---- row kernels (nkilab/kernels/norm.py) ------------------------------------- */
 
 /* y = x * rsqrt(mean(x^2) + eps) * weight, fp32 statistics, one HBM pass.

@@ -14,6 +14,10 @@ char* last_error_buffer() {
   return buf;
 }
 
+// SMs the persistent kernels of the calling host thread may fill (0: all); see
+// nkl_set_sm_budget.
+thread_local int g_sm_budget = 0;
+
 int sm_count() {
   static std::atomic<int> cached[64] = {};  // per device, filled once (idempotent)
   int dev = 0;
@@ -23,7 +27,7 @@ int sm_count() {
     if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
     cached[dev].store(n, std::memory_order_relaxed);
   }
-  return n;
+  return (g_sm_budget > 0 && g_sm_budget < n) ? g_sm_budget : n;
 }
 
 }  // namespace nkl
@@ -91,4 +95,11 @@ extern "C" int nkl_ipc_close(void* ptr) {
 extern "C" int nkl_ipc_free(void* ptr) {
   cudaError_t e = cudaFree(ptr);
   return e == cudaSuccess ? NKL_OK : nkl::fail(NKL_ERR_CUDA, "nkl_ipc_free: %s", cudaGetErrorString(e));
+}
+
+extern "C" int nkl_set_sm_budget(int sms, int* previous) {
+  if (sms < 0) return nkl::fail(NKL_ERR_ARG, "nkl_set_sm_budget: negative SM count %d", sms);
+  if (previous) *previous = nkl::g_sm_budget;
+  nkl::g_sm_budget = sms;
+  return NKL_OK;
 }

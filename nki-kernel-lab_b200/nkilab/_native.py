@@ -42,6 +42,7 @@ SIGNATURES = {
     "nkl_status_string": (ctypes.c_char_p, [_int]),
     "nkl_last_error": (ctypes.c_char_p, []),
     "nkl_check_device": (_int, [_p]),
+    "nkl_set_sm_budget": (_int, [_int, _p]),
     "nkl_rmsnorm": (_int, [_p, _p, _p, _i64, _i64, _f, _int, _p]),
     "nkl_add_rmsnorm": (_int, [_p, _p, _p, _p, _p, _i64, _i64, _f, _int, _p]),
     "nkl_softmax": (_int, [_p, _p, _i64, _i64, _int, _p]),

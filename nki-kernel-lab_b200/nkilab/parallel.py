@@ -359,24 +359,59 @@ class _Marks:
             self.record.append((name, ev))
 
 
+class sm_budget:
+    """Context manager: the persistent GEMM and attention kernels launched from this host
+    thread fill at most `sms` SMs (nkl_set_sm_budget; 0 = all), leaving the rest to kernels
+    that run beside them, such as NCCL's."""
+
+    def __init__(self, sms: int):
+        self.sms = sms
+        self.prev = 0
+
+    def __enter__(self):
+        from . import _native as N
+
+        prev = ctypes.c_int(0)
+        N.call("nkl_set_sm_budget", self.sms, ctypes.byref(prev))
+        self.prev = prev.value
+        return self
+
+    def __exit__(self, *exc):
+        from . import _native as N
+
+        N.call("nkl_set_sm_budget", self.prev, None)
+
+
 def decoder_block_overlapped(block, x: torch.Tensor, weights: Optional[ShardedBlockWeights] = None,
-                             group=None) -> torch.Tensor:
+                             group=None, comm_sms: int = 0) -> torch.Tensor:
     """decoder_block for x [B, S, d] bf16 on CUDA with the collectives overlapped with the
     GEMMs: the batch elements go through the block one after another, each one's row
     all-gathers and fp32 reduce-scatters issued asynchronously (NCCL's stream) while the
     next element's projections and attention run. Rows are sharded per batch element
     (rank r holds rows shard_range(S, world, r) of every element, S % world == 0); every
     kernel, rounding point and fp32 reduction is that of decoder_block, row for row.
-    Falls back to decoder_block when the shape does not allow it."""
+    With comm_sms > 0 the GEMM and attention grids leave that many SMs free (sm_budget)
+    for NCCL's kernels; the result then equals decoder_block run under the same budget
+    (the budget changes the attention's split-KV plan, and with it the rounding of split
+    query tiles). On two B200s at B=4, S=4096, d=4096 that made the block slower (4.29 ms
+    with all SMs, 4.42 ms with 16 left free, 4.50 ms with 32), so the default keeps every
+    SM. Falls back to decoder_block when the shape does not allow it."""
     world, rank = _world(group)
     B = x.shape[0] if x.dim() == 3 else 1
     cfg = block.cfg
     if (world == 1 or x.dim() != 3 or B < 2 or x.shape[1] % world or not x.is_cuda
             or x.dtype != torch.bfloat16 or cfg.head_dim not in (64, 128)):
         return decoder_block(block, x, weights=weights, group=group)
-    _, S, d = x.shape
-    hd = cfg.head_dim
     w = weights or shard_block(block, world, rank, x.dtype, x.device)
+    sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+    with sm_budget(max(1, sms - comm_sms) if comm_sms > 0 else 0):
+        return _overlapped(block, x, w, group, world, rank)
+
+
+def _overlapped(block, x: torch.Tensor, w: ShardedBlockWeights, group, world: int, rank: int) -> torch.Tensor:
+    cfg = block.cfg
+    B, S, d = x.shape
+    hd = cfg.head_dim
     nh = w.heads[1] - w.heads[0]
     s0, s1 = shard_range(S, world, rank)
     bf, f32 = torch.bfloat16, torch.float32

@@ -113,3 +113,26 @@ def test_attention_strided_rejects_bad_strides_before_device_work(native):
     assert call(kh=0) == native.ERR_ALIGN
     assert call(oh=-128) == native.ERR_ALIGN
     assert call(os_=64) == native.ERR_SHAPE
+
+
+def test_sm_budget_is_per_thread_and_returns_the_previous_value(native):
+    """nkl_set_sm_budget is host state only: it needs no GPU, it reports the value it
+    replaces, rejects negative counts and is kept per host thread."""
+    import threading
+
+    L = native.lib
+    prev = ctypes.c_int(-1)
+    assert L.nkl_set_sm_budget(100, ctypes.byref(prev)) == native.OK and prev.value == 0
+    seen = []
+
+    def other():
+        p = ctypes.c_int(-1)
+        L.nkl_set_sm_budget(7, ctypes.byref(p))
+        seen.append(p.value)
+
+    t = threading.Thread(target=other)
+    t.start()
+    t.join()
+    assert seen == [0]  # another thread starts from "all SMs"
+    assert L.nkl_set_sm_budget(-1, None) == native.ERR_ARG
+    assert L.nkl_set_sm_budget(0, ctypes.byref(prev)) == native.OK and prev.value == 100

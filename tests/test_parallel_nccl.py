@@ -92,9 +92,18 @@ def _worker(rank: int, world: int, port: int) -> None:
             o32, o64 = _oracle_pair(block, xb[b_i])
             assert_block_parity(got_b[b_i].float().cpu().numpy(), o32, o64)
         # the same block with the collectives overlapped per batch element: the same kernels
-        # row for row and two-rank fp32 sums, so the same bits
-        got_o = P.decoder_block_overlapped(block, xb.to(dev), weights=w)
+        # row for row and two-rank fp32 sums, so the same bits when no SMs are set aside ...
+        got_o = P.decoder_block_overlapped(block, xb.to(dev), weights=w, comm_sms=0)
         assert torch.equal(got_o, got_b)
+        # ... and, with 16 SMs left to NCCL, the bits of the serial block under that budget
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        got_o = P.decoder_block_overlapped(block, xb.to(dev), weights=w, comm_sms=16)
+        with P.sm_budget(sms - 16):
+            got_s = P.decoder_block(block, xb.to(dev), weights=w)
+        assert torch.equal(got_o, got_s)
+        for b_i in range(2):
+            o32, o64 = _oracle_pair(block, xb[b_i])
+            assert_block_parity(got_o[b_i].float().cpu().numpy(), o32, o64)
         dist.barrier()
     finally:
         dist.destroy_process_group()
