@@ -506,7 +506,8 @@ def bench_ladder(dev, stream, pk) -> dict:
       attention 8x2048x128: naive (scores and probabilities through HBM) -> flash, one
       query tile per CTA, no split (flash / flash_kv_resident) -> the same kernel with
       causal key ranges split over all SMs (flash_balanced; the default) -> two query
-      tiles per CTA interleaved (flash_pipelined's ILP = 2)
+      tiles per CTA interleaved (flash_pipelined's ILP = 2) -> one query tile, two softmax
+      groups on alternate key tiles
       softmax [4096, 2048]: unfused (3 HBM passes) -> fused; GEMM 1024^3: naive -> blocked."""
     from nkilab import _native as N
 
@@ -519,7 +520,7 @@ def bench_ladder(dev, stream, pk) -> dict:
     st = stream.cuda_stream
     att = {}
     for name, mode in (("flash_one_tile_unsplit", N.ATTN_ONE_TILE_UNSPLIT), ("flash_split_kv_default", N.ATTN_AUTO),
-                       ("flash_two_tile", N.ATTN_TWO_TILE)):
+                       ("flash_two_tile", N.ATTN_TWO_TILE), ("flash_two_softmax_groups", N.ATTN_TWO_GROUPS)):
         nbytes = N.lib.nkl_attention_mode_workspace_size(H, S, D, N.BFLOAT16, mode)
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
 
@@ -829,7 +830,8 @@ def run_ours(args, ctx) -> None:
     print(json.dumps(line), flush=True)
 
 
-PROFILE_CASES = ("rmsnorm", "softmax", "swiglu", "gemm1024", "gemm8192", "attention", "attention_two_tile")
+PROFILE_CASES = ("rmsnorm", "softmax", "swiglu", "gemm1024", "gemm8192", "attention", "attention_two_tile",
+                 "attention_two_groups")
 
 
 def run_profile_case(case: str, launches: int, rows: int = ROWS) -> None:
@@ -865,7 +867,7 @@ def run_profile_case(case: str, launches: int, rows: int = ROWS) -> None:
     else:
         q, k, v = (torch.randn(H, S, D, device=dev, generator=g).to(bf) for _ in range(3))
         o = torch.empty_like(q)
-        mode = N.ATTN_TWO_TILE if case == "attention_two_tile" else N.ATTN_AUTO
+        mode = {"attention_two_tile": N.ATTN_TWO_TILE, "attention_two_groups": N.ATTN_TWO_GROUPS}.get(case, N.ATTN_AUTO)
         nbytes = N.lib.nkl_attention_mode_workspace_size(H, S, D, N.BFLOAT16, mode)
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=dev)
         for _ in range(launches):

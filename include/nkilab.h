@@ -244,18 +244,24 @@ int nkl_attention_strided(const void* q, const void* k, const void* v, void* out
 
 /* Launch modes of the bf16 flash kernels, the B200 rungs of the reference's flash ladder
  * (nkilab/kernels/attention.py:155-325, README.md:17-23):
- *   NKL_ATTN_AUTO             what nkl_attention_ws runs: one 128-row query tile per CTA
- *                             with S double buffered in TMEM, causal key ranges split over
+ *   NKL_ATTN_AUTO             what nkl_attention_ws runs: one 128-row query tile per CTA,
+ *                             Q and P in TMEM (A operands), S double buffered in TMEM, every
+ *                             score row split over two warps; causal key ranges split over
  *                             all SMs where that balances the work (flash_balanced's goal)
  *   NKL_ATTN_ONE_TILE_UNSPLIT the same kernel with every query tile in one unit, no
  *                             workspace (flash / flash_kv_resident: K and V reused from L2)
  *   NKL_ATTN_TWO_TILE         two query tiles per CTA interleaved on the tensor core and two
  *                             softmax warp groups (flash_pipelined's ILP = 2 interleave);
  *                             head_dim 128, seq a multiple of 256
+ *   NKL_ATTN_TWO_GROUPS       one query tile per CTA with two softmax warp groups taking
+ *                             alternate key tiles (the running max handed from one to the
+ *                             other), one O accumulator each, P through shared memory so S is
+ *                             released as soon as it is loaded; the NKL_ATTN_AUTO split plan
  * Every mode computes the same softmax with the reference's rounding points. */
 #define NKL_ATTN_AUTO 0
 #define NKL_ATTN_ONE_TILE_UNSPLIT 1
 #define NKL_ATTN_TWO_TILE 2
+#define NKL_ATTN_TWO_GROUPS 3
 
 /* Workspace bytes nkl_attention_mode uses for this shape and mode (0: none needed). */
 size_t nkl_attention_mode_workspace_size(int64_t heads, int64_t seq, int64_t head_dim, int dtype, int mode);

@@ -29,8 +29,12 @@
 //   warp 8     TMA producer: Q per unit (double buffered), K and V through 2-deep rings
 //   warp 9     TMEM allocator + single-thread tcgen05.mma issuer. S is double buffered
 //              in TMEM: S(t+2) = Q K(t+2)^T is issued right behind O += P(t) V(t), so the
-//              tensor core computes the next tile's scores while the engine exponentiates
-//   TMEM       S/P buffers [0,128) and [128,256), O [256, 256+d)
+//              tensor core computes the next tile's scores while the engine exponentiates.
+//              Both products take their A operand from TMEM (Q and P), so shared memory
+//              only supplies K and V to the tensor core; the engine copies each unit's Q
+//              from shared memory into TMEM before the previous unit's epilogue
+//   TMEM       S/P buffers [0,128) and [128,256), O [256, 256+d), Q [256+d, 256+2d) (two
+//              buffers of d/2 columns of bf16 pairs)
 //   epilogue   O from TMEM, * 1/l, bf16, staged in the unit's Q buffer, TMA store
 #include <algorithm>
 #include <map>
@@ -141,6 +145,7 @@ struct AttnSmem {
   uint64_t pv_step;    // one phase per P.V tile
   uint64_t pv_done;    // one phase per unit: its last P.V complete
   uint64_t o_free;     // engine has read O (all engine threads)
+  uint64_t qt_full[2];  // Q of the unit copied into TMEM buffer u & 1 (all engine threads)
   uint64_t mma_done;
   float xmax[2][2 * kTile];  // [tile parity][half * 128 + row]: row-max exchange
   float xsum[2 * kTile];     // [half * 128 + row]: row-sum exchange
@@ -267,6 +272,78 @@ __device__ __forceinline__ bool next_unit(const AttnArgs& a, int i, UnitRun& r) 
   return true;
 }
 
+// TMA producer (one warp): per unit, in the order the MMA warp consumes them: K(0), Q,
+// K(1), then V(t) followed by K(t+2); Q double buffered, K and V through 2-deep rings.
+// Shared by the flash kernels whose shared-memory layout names these buffers and barriers.
+template <int D, class Smem>
+__device__ __forceinline__ void attn_produce(Smem& s, const CUtensorMap* map_q, const CUtensorMap* map_k,
+                                             const CUtensorMap* map_v, const AttnArgs& args) {
+  constexpr uint32_t kTileBytes = kTile * D * 2;
+  constexpr int kSub = D / 64;
+  if (elect_one()) {
+    uint32_t kc = 0, vc = 0, qc = 0;
+    int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1}, q_armed[2] = {-1, -1};
+    bool ok = true;
+    UnitRun un;
+    // Key / value tile `kt` (absolute key-tile index) of kv head `kvh`.
+    auto load_k = [&](int kt, int kvh) -> bool {
+      const int ks = kc & 1;
+      if (!mbar_wait(&s.k_empty[ks], ((kc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 11)) return false;
+      mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
+      k_armed[ks] = (int)((kc >> 1) & 1u);
+      for (int c = 0; c < kSub; ++c)
+        tma_load_3d(s.k[ks] + c * (kTile * 128), map_k, &s.k_full[ks], c * 64, kt * kTile, kvh);
+      ++kc;
+      return true;
+    };
+    auto load_v = [&](int kt, int kvh) -> bool {
+      const int vs = vc & 1;
+      if (!mbar_wait(&s.v_empty[vs], ((vc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 12)) return false;
+      mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
+      v_armed[vs] = (int)((vc >> 1) & 1u);
+      for (int c = 0; c < kSub; ++c)
+        tma_load_3d(s.v[vs] + c * (kTile * 128), map_v, &s.v_full[vs], c * 64, kt * kTile, kvh);
+      ++vc;
+      return true;
+    };
+    // Per unit, in the order the MMA warp consumes them: K(0), Q, K(1), then V(t)
+    // followed by K(t+2).
+    for (int i = 0; ok && next_unit(args, i, un); ++i) {
+      const int j0 = un.j0, kvh = un.kv_head;
+      ok = load_k(j0, kvh);
+      if (ok) {
+        const int qb = qc & 1;
+        if (!mbar_wait(&s.q_empty[qb], ((qc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&s.q_full[qb], kTileBytes);
+        q_armed[qb] = (int)((qc >> 1) & 1u);
+        for (int c = 0; c < kSub; ++c)
+          tma_load_3d(s.q[qb] + c * (kTile * 128), map_q, &s.q_full[qb], c * 64, un.qt * kTile, un.head);
+        ++qc;
+      }
+      if (ok && un.n > 1) ok = load_k(j0 + 1, kvh);
+      for (int t = 0; ok && t < un.n; ++t) {
+        ok = load_v(j0 + t, kvh);
+        if (ok && t + 2 < un.n) ok = load_k(j0 + t + 2, kvh);
+      }
+    }
+    if (!ok) {  // let issued copies land before shared memory is released
+      const uint64_t t0 = globaltimer();
+      for (int b = 0; b < 2; ++b) {
+        if (q_armed[b] >= 0)
+          while (!mbar_try_wait(&s.q_full[b], (uint32_t)q_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+        if (k_armed[b] >= 0)
+          while (!mbar_try_wait(&s.k_full[b], (uint32_t)k_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+        if (v_armed[b] >= 0)
+          while (!mbar_try_wait(&s.v_full[b], (uint32_t)v_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
+      }
+    }
+  }
+  __syncwarp();  // the warp reconverges here: the CTA barrier below must see all 32 lanes
+}
+
 template <int D>
 __global__ void __launch_bounds__(kAttnThreads, 1)
 attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -283,10 +360,11 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
   auto& s = *reinterpret_cast<AttnSmem<D>*>(smem_raw);
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kOCol0 = 2 * kTile;  // S/P buffers at [0,128) and [128,256)
+  constexpr uint32_t kQtCol0 = kOCol0 + D;  // Q buffers (bf16 pairs) at kQtCol0 + b * D / 2
   constexpr uint32_t kIdescS = idesc_bf16_f32(kTile, kTile, false, false);
   constexpr uint32_t kIdescPV = idesc_bf16_f32(kTile, D, false, true);
-  constexpr uint32_t kTileBytes = kTile * D * 2;
   constexpr int kSub = D / 64;  // 64-column (128-byte) sub-tiles per Q/K/V tile
+  static_assert(kQtCol0 + D <= kTmemCols, "TMEM columns");
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -302,6 +380,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.p_full[i], kEngineThreads);
+      mbar_init(&s.qt_full[i], kEngineThreads);
     }
     mbar_init(&s.pv_step, 1);
     mbar_init(&s.pv_done, 1);
@@ -345,87 +424,25 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
 
   if (warp == kProducerWarp) {
     // ------------------------------------------------ TMA producer
-    if (elect_one()) {
-      uint32_t kc = 0, vc = 0, qc = 0;
-      int k_armed[2] = {-1, -1}, v_armed[2] = {-1, -1}, q_armed[2] = {-1, -1};
-      bool ok = true;
-      UnitRun un;
-      // Key / value tile `kt` (absolute key-tile index) of kv head `kvh`.
-      auto load_k = [&](int kt, int kvh) -> bool {
-        const int ks = kc & 1;
-        if (!mbar_wait(&s.k_empty[ks], ((kc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 11)) return false;
-        mbar_arrive_expect_tx(&s.k_full[ks], kTileBytes);
-        k_armed[ks] = (int)((kc >> 1) & 1u);
-        for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.k[ks] + c * (kTile * 128), &map_k, &s.k_full[ks], c * 64, kt * kTile, kvh);
-        ++kc;
-        return true;
-      };
-      auto load_v = [&](int kt, int kvh) -> bool {
-        const int vs = vc & 1;
-        if (!mbar_wait(&s.v_empty[vs], ((vc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 12)) return false;
-        mbar_arrive_expect_tx(&s.v_full[vs], kTileBytes);
-        v_armed[vs] = (int)((vc >> 1) & 1u);
-        for (int c = 0; c < kSub; ++c)
-          tma_load_3d(s.v[vs] + c * (kTile * 128), &map_v, &s.v_full[vs], c * 64, kt * kTile, kvh);
-        ++vc;
-        return true;
-      };
-      // Per unit, in the order the MMA warp consumes them: K(0), Q, K(1), then V(t)
-      // followed by K(t+2).
-      for (int i = 0; ok && next_unit(args, i, un); ++i) {
-        const int j0 = un.j0, kvh = un.kv_head;
-        ok = load_k(j0, kvh);
-        if (ok) {
-          const int qb = qc & 1;
-          if (!mbar_wait(&s.q_empty[qb], ((qc >> 1) & 1u) ^ 1u, &s.abort, &g_attn_dev_error, 10)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_expect_tx(&s.q_full[qb], kTileBytes);
-          q_armed[qb] = (int)((qc >> 1) & 1u);
-          for (int c = 0; c < kSub; ++c)
-            tma_load_3d(s.q[qb] + c * (kTile * 128), &map_q, &s.q_full[qb], c * 64, un.qt * kTile, un.head);
-          ++qc;
-        }
-        if (ok && un.n > 1) ok = load_k(j0 + 1, kvh);
-        for (int t = 0; ok && t < un.n; ++t) {
-          ok = load_v(j0 + t, kvh);
-          if (ok && t + 2 < un.n) ok = load_k(j0 + t + 2, kvh);
-        }
-      }
-      if (!ok) {  // let issued copies land before shared memory is released
-        const uint64_t t0 = globaltimer();
-        for (int b = 0; b < 2; ++b) {
-          if (q_armed[b] >= 0)
-            while (!mbar_try_wait(&s.q_full[b], (uint32_t)q_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-          if (k_armed[b] >= 0)
-            while (!mbar_try_wait(&s.k_full[b], (uint32_t)k_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-          if (v_armed[b] >= 0)
-            while (!mbar_try_wait(&s.v_full[b], (uint32_t)v_armed[b]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-        }
-      }
-    }
-    __syncwarp();  // the warp reconverges here: the CTA barrier below must see all 32 lanes
+    attn_produce<D>(s, &map_q, &map_k, &map_v, args);
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------ MMA issuer
     if (elect_one()) {
       uint32_t kc = 0, vc = 0, qc = 0, gt = 0, uc = 0;
-      const uint64_t q_desc0 = smem_desc_sw128(smem_u32(s.q[0]), 16, 1024);
-      const uint64_t q_desc1 = smem_desc_sw128(smem_u32(s.q[1]), 16, 1024);
       const uint64_t k_desc0 = smem_desc_sw128(smem_u32(s.k[0]), 16, 1024);
       const uint64_t k_desc1 = smem_desc_sw128(smem_u32(s.k[1]), 16, 1024);
       const uint64_t v_desc0 = smem_desc_sw128(smem_u32(s.v[0]), kTile * 128, 1024);
       const uint64_t v_desc1 = smem_desc_sw128(smem_u32(s.v[1]), kTile * 128, 1024);
       bool ok = true;
       // S into TMEM buffer b from Q buffer qb and K stage ks
+      // S into TMEM buffer b from the unit's Q in TMEM buffer qb (A operand) and K stage ks
       auto issue_s = [&](int qb, int ks, int b) {
-        const uint64_t qd = qb ? q_desc1 : q_desc0;
         const uint64_t kd = ks ? k_desc1 : k_desc0;
+        const uint32_t qt = tmem + kQtCol0 + (uint32_t)(qb * (D / 2));
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(((kk >> 2) * (kTile * 128) + (kk & 3) * 32) >> 4);
-          mma_bf16_ss(tmem + (uint32_t)(b * kTile), qd + off, kd + off, kIdescS, kk > 0 ? 1u : 0u);
+          mma_bf16_ts(tmem + (uint32_t)(b * kTile), qt + (uint32_t)(kk * 8), kd + off, kIdescS, kk > 0 ? 1u : 0u);
         }
         mma_commit(&s.s_full[b]);
       };
@@ -433,7 +450,8 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       for (int i = 0; ok && next_unit(args, i, un); ++i) {
         const int n = un.n;
         const int qb = qc & 1;
-        if (!mbar_wait(&s.q_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
+        // the engine has copied the unit's Q from shared memory into TMEM buffer qb
+        if (!mbar_wait(&s.qt_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
         ++qc;
         for (int t = 0; t < n && t < 2; ++t) {  // S for the unit's first two key tiles
           const uint32_t ki = kc + (uint32_t)t;
@@ -500,7 +518,38 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     bool stored_any = false;
     uint32_t gt = 0, uc = 0;
     bool ok = true;
+    // Q of the unit with count c: from its shared-memory buffer c & 1 (128-byte-swizzled
+    // rows) into TMEM buffer c & 1 as the A operand of Q K^T (row r in lane r, bf16 pairs
+    // (2j, 2j+1) in column j); this warp copies its lane quadrant's rows, half hf of the
+    // columns.
+    auto copy_q = [&](uint32_t c) -> bool {
+      const int qb = c & 1;
+      if (!warp_wait(&s.q_full[qb], (c >> 1) & 1u, &s.abort, 30)) return false;
+      constexpr int kChunks = D / 16;  // 16-byte chunks of the row per warp half
+      uint32_t w[kChunks * 4];
+#pragma unroll
+      for (int j2 = 0; j2 < kChunks; ++j2) {
+        const int j = hf * kChunks + j2;  // chunk of the row: sub-tile j / 8, chunk j % 8
+        const uint4 x = *reinterpret_cast<const uint4*>(s.q[qb] + (j / 8) * (kTile * 128) + r * 128 +
+                                                         (((j & 7) ^ sw) * 16));
+        w[4 * j2] = x.x;
+        w[4 * j2 + 1] = x.y;
+        w[4 * j2 + 2] = x.z;
+        w[4 * j2 + 3] = x.w;
+      }
+      const uint32_t dst = tmem + lane_off + kQtCol0 + (uint32_t)(qb * (D / 2) + hf * (D / 4));
+      if constexpr (D == 128) {
+        tmem_st32(dst, w);
+      } else {
+        tmem_st16(dst, *reinterpret_cast<const uint32_t(*)[16]>(w));
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&s.qt_full[qb]);
+      return true;
+    };
     UnitRun un;
+    if (next_unit(args, 0, un)) ok = copy_q(0);
     for (int i = 0; ok && next_unit(args, i, un); ++i) {
       const int u = un.u;
       const int qt = un.qt;
@@ -563,6 +612,12 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         l = l * factor + rs;
       }
       if (!ok) break;
+      // the next unit's Q into the other TMEM buffer, so its first scores are computed
+      // while this unit's epilogue runs
+      {
+        UnitRun nx;
+        if (next_unit(args, i + 1, nx) && !copy_q(uc + 1)) { ok = false; break; }
+      }
       // ---------------- epilogue: O (complete after the unit's last P.V) -> output or partial
       if (!warp_wait(&s.pv_done, uc & 1u, &s.abort, 33)) { ok = false; break; }
       tc_fence_after();
@@ -731,6 +786,7 @@ __global__ void __launch_bounds__(64) attn_combine_bf16_kernel(const __grid_cons
 }
 
 #include "attention_pair.cuh"
+#include "attention_pp.cuh"
 
 // ------------------------------------------------------------------ fp32 exact flash kernel
 // CUDA-core flash attention for fp32 inputs (the reference's fp32 tests need 2e-5
@@ -1058,7 +1114,8 @@ struct PeerDest {
   int n = 0, heads_total = 0, head_offset = 0;
 };
 
-template <int D>
+// PP: the two-softmax-group kernel (attn_fwd_pp_bf16_kernel), else attn_fwd_bf16_kernel.
+template <int D, bool PP>
 int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int heads, int kv_heads, int seq,
                      float scale, void* ws, size_t ws_bytes, const AttnLayout& lay, cudaStream_t st,
                      const PeerDest* pd = nullptr) {
@@ -1077,12 +1134,14 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   const AttnPlan& plan = cached_plan(heads, heads / kv_heads, seq, D, ws != nullptr);
   if (plan.ws_bytes > 0 && ws_bytes < plan.ws_bytes)
     return fail(NKL_ERR_ARG, "nkl_attention_ws: workspace %zu B < required %zu B", ws_bytes, plan.ws_bytes);
-  constexpr size_t smem = attn_smem_bytes<D>();
+  constexpr size_t smem = PP ? sizeof(PPSmem<D>) : attn_smem_bytes<D>();
+  static_assert(smem <= 232448, "attention kernel shared memory above the 227 KB per-block limit");
+  constexpr auto kernel = PP ? attn_fwd_pp_bf16_kernel<D> : attn_fwd_bf16_kernel<D>;
   static std::atomic<bool> attr_set[64] = {};  // per device: the smem attribute is set (idempotent)
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || !attr_set[dev].load(std::memory_order_acquire)) {
-    cudaError_t e = cudaFuncSetAttribute(attn_fwd_bf16_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return fail(NKL_ERR_CUDA, "nkl_attention: %s", cudaGetErrorString(e));
     if (dev >= 0 && dev < 64) attr_set[dev].store(true, std::memory_order_release);
   }
@@ -1100,7 +1159,7 @@ int launch_attn_bf16(const void* q, const void* k, const void* v, void* out, int
   a.n_ctas_listed = plan.cta_off.empty() ? 0 : plan.ctas;
   for (size_t i = 0; i < plan.cta_off.size(); ++i) a.cta_off[i] = plan.cta_off[i];
   for (size_t i = 0; i < plan.unit_desc.size(); ++i) a.unit_desc[i] = plan.unit_desc[i];
-  rc = launch_pdl(attn_fwd_bf16_kernel<D>, dim3(plan.ctas), dim3(kAttnThreads), smem, st, "nkl_attention", mq, mk, mv,
+  rc = launch_pdl(kernel, dim3(plan.ctas), dim3(PP ? kPPThreads : kAttnThreads), smem, st, "nkl_attention", mq, mk, mv,
                   mo, a, peers);
   if (rc || plan.jobs.empty()) return rc;
   // split query tiles: merge the partials (programmatic dependent launch: the combine
@@ -1449,11 +1508,13 @@ int attention_impl(const char* op, const void* q, const void* k, const void* v, 
                                       workspace ? workspace_bytes : 0, lay, st);
   }
   if (mode == NKL_ATTN_ONE_TILE_UNSPLIT) workspace = nullptr;
-  if (head_dim == 64)
-    return launch_attn_bf16<64>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                                workspace ? workspace_bytes : 0, lay, st, peers);
-  return launch_attn_bf16<128>(q, k, v, out, (int)heads, (int)kv_heads, (int)seq, scale, workspace,
-                               workspace ? workspace_bytes : 0, lay, st, peers);
+  const size_t wsb = workspace ? workspace_bytes : 0;
+  const int h = (int)heads, kvh = (int)kv_heads, n = (int)seq;
+  if (mode == NKL_ATTN_TWO_GROUPS)
+    return head_dim == 64 ? launch_attn_bf16<64, true>(q, k, v, out, h, kvh, n, scale, workspace, wsb, lay, st, peers)
+                          : launch_attn_bf16<128, true>(q, k, v, out, h, kvh, n, scale, workspace, wsb, lay, st, peers);
+  return head_dim == 64 ? launch_attn_bf16<64, false>(q, k, v, out, h, kvh, n, scale, workspace, wsb, lay, st, peers)
+                        : launch_attn_bf16<128, false>(q, k, v, out, h, kvh, n, scale, workspace, wsb, lay, st, peers);
 }
 
 }  // namespace
@@ -1557,7 +1618,8 @@ extern "C" size_t nkl_attention_mode_workspace_size(int64_t heads, int64_t seq, 
 extern "C" int nkl_attention_mode(const void* q, const void* k, const void* v, void* out, void* workspace,
                                   size_t workspace_bytes, int64_t heads, int64_t seq, int64_t head_dim, float scale,
                                   int dtype, int mode, void* stream) {
-  if (mode != NKL_ATTN_AUTO && mode != NKL_ATTN_ONE_TILE_UNSPLIT && mode != NKL_ATTN_TWO_TILE)
+  if (mode != NKL_ATTN_AUTO && mode != NKL_ATTN_ONE_TILE_UNSPLIT && mode != NKL_ATTN_TWO_TILE &&
+      mode != NKL_ATTN_TWO_GROUPS)
     return fail(NKL_ERR_ARG, "nkl_attention_mode: unknown mode %d", mode);
   if (mode == NKL_ATTN_TWO_TILE && dtype != NKL_BFLOAT16)
     return fail(NKL_ERR_DTYPE, "nkl_attention_mode: the two-query-tile kernel is bf16 only");

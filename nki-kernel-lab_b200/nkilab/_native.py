@@ -20,6 +20,7 @@ BFLOAT16 = 1
 ATTN_AUTO = 0
 ATTN_ONE_TILE_UNSPLIT = 1
 ATTN_TWO_TILE = 2
+ATTN_TWO_GROUPS = 3
 
 # status codes (nkl_status)
 OK = 0

@@ -46,7 +46,7 @@ def _inputs(H, S, D=128, seed=0, scale=1.0):
 
 
 @pytest.mark.parametrize("H,S", [(8, 2048), (1, 4096), (4, 768)])
-@pytest.mark.parametrize("mode", [0, 1, 2])
+@pytest.mark.parametrize("mode", [0, 1, 2, 3])
 def test_modes_match_oracle(H, S, mode):
     q, k, v = _inputs(H, S, seed=H + S)
     out, _ = _run(*(t.cuda() for t in (q, k, v)), mode)
@@ -63,8 +63,8 @@ def test_unsplit_kernel_follows_the_reference_rounding():
     o64 = O.attention_flash(q, k, v, acc=torch.float64).float()
     floor_diff = float(((o32 - o64).abs() > 0).float().mean())
     floor_mean = float((o32 - o64).abs().mean())
-    for mode in (1, 2):  # every query tile in one unit: no chunk-local maxima
-        out = _run(*(t.cuda() for t in (q, k, v)), mode)[0] if mode == 1 else _run_two_tile_unsplit(q, k, v)
+    for mode in (1, 2, 3):  # every query tile in one unit: no chunk-local maxima
+        out = _run(*(t.cuda() for t in (q, k, v)), mode)[0] if mode == 1 else _run_unsplit(q, k, v, mode)
         d = (out.float().cpu() - o64).abs()
         diff, mean = float((d > 0).float().mean()), float(d.mean())
         msg = (f"mode {mode}: differing {diff:.2e} vs fp32 oracle {floor_diff:.2e}; "
@@ -73,8 +73,8 @@ def test_unsplit_kernel_follows_the_reference_rounding():
         assert mean <= 1.5 * floor_mean + 1e-8, msg
 
 
-def _run_two_tile_unsplit(q, k, v):
-    """The two-tile kernel without a workspace: its plan keeps every pair in one unit."""
+def _run_unsplit(q, k, v, mode):
+    """A kernel run without a workspace: its plan keeps every query tile (pair) in one unit."""
     from nkilab import _native as N
 
     qd, kd, vd = (t.cuda() for t in (q, k, v))
@@ -82,8 +82,8 @@ def _run_two_tile_unsplit(q, k, v):
     o = torch.full_like(qd, float("nan"))
     p = lambda t: ctypes.c_void_p(t.data_ptr())  # noqa: E731
     st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
-    rc = N.lib.nkl_attention_mode(p(qd), p(kd), p(vd), p(o), None, 0, H, S, D, 1.0 / math.sqrt(D), N.BFLOAT16,
-                                  N.ATTN_TWO_TILE, st)
+    rc = N.lib.nkl_attention_mode(p(qd), p(kd), p(vd), p(o), None, 0, H, S, D, 1.0 / math.sqrt(D), N.BFLOAT16, mode,
+                                  st)
     assert rc == N.OK, N.lib.nkl_last_error()
     torch.cuda.synchronize()
     return o
