@@ -427,7 +427,9 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         serial = lambda marks=None: P.decoder_block(block, x, weights=w, marks=marks)  # noqa: E731
         fwd = lambda: P.decoder_block_overlapped(block, x, weights=w)  # noqa: E731
         out["parallelism"] = (f"tp{world} heads x ffn columns, sequence-parallel rows, fp32 reduce-scatter; "
-                              "collectives of each batch element overlapped with the next one's GEMMs")
+                              + ("collectives of each batch element overlapped with the next one's GEMMs"
+                                 if world < 4 else "serial (parallel.decoder_block_overlapped falls back to it "
+                                                   "from four ranks on)"))
         with torch.cuda.stream(stream):
             y = fwd()
             torch.cuda.synchronize()
@@ -457,7 +459,7 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         ms = ctx["max"](t0.elapsed_time(t1) / steps)
         if world > 1:  # SMs left to NCCL while the overlapped block's GEMMs run
             by_sms = {}
-            for c in (16, 32):
+            for c in ((16, 32) if world < 4 else ()):
                 ctx["barrier"]()
                 P.decoder_block_overlapped(block, x, weights=w, comm_sms=c)
                 torch.cuda.synchronize()
@@ -743,8 +745,12 @@ def run_ours(args, ctx) -> None:
     extra_err = {}
     parity = sharded_parity(dev, ctx) if world > 1 else None
     with ClockSampler(ctx["local"]) as clk:
-        att = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx)
-        att_nccl = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx, gather="nccl") if world > 1 else None
+        from nkilab import parallel as P
+
+        gather = P.preferred_gather(world)
+        other = "nccl" if gather == "nvlink" else "nvlink"
+        att = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx, gather=gather)
+        att_other = bench_attention_sharded(args.steps, args.warmup, dev, stream, ctx, gather=other) if world > 1 else None
         rep = bench_attention(args.steps, args.warmup, dev, stream, ctx) if world > 1 else None
         rows = gemm = block = ladder = None
         if not args.headline_only:
@@ -785,7 +791,9 @@ def run_ours(args, ctx) -> None:
         "config": {"workload": "causal attention 8x2048x128 bf16, scale 1/sqrt(128) (BASELINE configs[3])",
                    "heads": H, "seq_len": S, "head_dim": D, "batch": 1,
                    "parallelism": (f"heads sharded over {world} GPUs ({att['heads_per_rank']} per rank); the output "
-                                   "gathered to every rank over NVLink by the attention kernels, in the timed region")
+                                   + ("gathered to every rank over NVLink by the attention kernels"
+                                      if gather == "nvlink" else "gathered to every rank by an NCCL all-gather")
+                                   + " in the timed region (parallel.preferred_gather)")
                    if world > 1 else "single",
                    "l2": f"rotating pool of {att['pool_sets']} input sets, {att['pool_mib']:.0f} MiB > 2x L2",
                    "launch": "K steps in one CUDA graph via torch.ops.nkilab.attention (+ all-gather)"},
@@ -795,7 +803,8 @@ def run_ours(args, ctx) -> None:
                      "algorithmic_flop_per_launch": ATTN_FLOP / world, "peak_source": pk["source"] + " burst bf16",
                      "kernel": "attn_fwd_bf16_kernel<128>",
                      "timed_over": "the whole op per step (attention kernel + split-KV combine kernel"
-                                   + (" + the NVLink gather and flag exchange" if world > 1 else "")
+                                   + ((" + the NVLink gather and flag exchange" if gather == "nvlink"
+                                       else " + the NCCL all-gather") if world > 1 else "")
                                    + "), per GPU, so 'achieved' is a lower bound for the attention kernel alone"},
         "clocks": clocks,
         "e2e": e2e,
@@ -803,12 +812,14 @@ def run_ours(args, ctx) -> None:
         "step_us_spread": att["us_per_step_rank0"],
     }
     if world > 1:
-        line["sharded"] = {"gather": "attention kernels store every output tile into every rank's buffer over NVLink "
-                                     "(parallel.PeerAttention), then a flag exchange",
-                           "attention_us": att["attention_us"], "gather_us": att["all_gather_us"],
-                           "heads_per_rank": att["heads_per_rank"], "parity": parity,
-                           "nccl_all_gather_instead": {"us_per_step": round(att_nccl["ms_per_step"] * 1e3, 3),
-                                                       "all_gather_us": att_nccl["all_gather_us"]}}
+        what = {"nvlink": "attention kernels store every output tile into every rank's buffer over NVLink "
+                          "(parallel.PeerAttention), then a flag exchange",
+                "nccl": "NCCL all-gather of the output after the attention kernels"}
+        line["sharded"] = {"gather": what[gather], "attention_us": att["attention_us"],
+                           "gather_us": att["all_gather_us"], "heads_per_rank": att["heads_per_rank"],
+                           "parity": parity,
+                           f"{other}_gather_instead": {"us_per_step": round(att_other["ms_per_step"] * 1e3, 3),
+                                                       "gather_us": att_other["all_gather_us"]}}
         rms = rep["ms_per_step"]
         line["replicas"] = {"value": round(ATTN_FLOP * world / (rms * 1e-3) / 1e12, 2), "unit": "TFLOPS",
                             "ms_per_step": round(rms, 5), "scaling": "weak",

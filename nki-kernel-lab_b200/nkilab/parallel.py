@@ -123,6 +123,16 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, variant: str = 
     return all_gather_dim0(local, H, group)
 
 
+def preferred_gather(world: int) -> str:
+    """How the head-sharded attention's output should reach every rank: "nvlink" (the
+    attention kernels store each output tile into every rank's buffer, PeerAttention) or
+    "nccl" (an all-gather after the kernels). Measured on B200s with 8 heads x 2048 x 128:
+    two GPUs 31.4 us per step over NVLink against 43.4 us with NCCL; eight GPUs 48.1 us
+    against 44.2 us (with one head per rank most output tiles come from the split-KV
+    combine kernel, whose stores to seven peers dominate)."""
+    return "nvlink" if world <= 2 else "nccl"
+
+
 class _RawCuda:
     """A device allocation seen through __cuda_array_interface__, so torch.as_tensor can
     view it without a copy (as uint16; the caller views it as bfloat16)."""
@@ -395,11 +405,15 @@ def decoder_block_overlapped(block, x: torch.Tensor, weights: Optional[ShardedBl
     (the budget changes the attention's split-KV plan, and with it the rounding of split
     query tiles). On two B200s at B=4, S=4096, d=4096 that made the block slower (4.29 ms
     with all SMs, 4.42 ms with 16 left free, 4.50 ms with 32), so the default keeps every
-    SM. Falls back to decoder_block when the shape does not allow it."""
+    SM. Falls back to decoder_block when the shape does not allow it, and with four or more
+    ranks."""
     world, rank = _world(group)
     B = x.shape[0] if x.dim() == 3 else 1
     cfg = block.cfg
-    if (world == 1 or x.dim() != 3 or B < 2 or x.shape[1] % world or not x.is_cuda
+    # With four or more ranks the per-element collectives are latency-bound and the serial
+    # block is faster (eight B200s at B=4, S=4096, d=4096: 2.44 ms serial against 2.87 ms
+    # overlapped; two: 5.06 ms serial against 4.29 ms overlapped).
+    if (world == 1 or world >= 4 or x.dim() != 3 or B < 2 or x.shape[1] % world or not x.is_cuda
             or x.dtype != torch.bfloat16 or cfg.head_dim not in (64, 128)):
         return decoder_block(block, x, weights=weights, group=group)
     w = weights or shard_block(block, world, rank, x.dtype, x.device)
