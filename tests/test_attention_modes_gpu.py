@@ -89,6 +89,16 @@ def _run_unsplit(q, k, v, mode):
     return o
 
 
+@pytest.mark.parametrize("mode", [0, 1, 3])
+@pytest.mark.parametrize("H,S", [(8, 1024), (3, 700)])
+def test_modes_head_dim_64_match_oracle(H, S, mode):
+    """head_dim 64 instantiations of the one-tile kernels (the two-tile kernel is 128 only)."""
+    q, k, v = _inputs(H, S, D=64, seed=H * S)
+    out, _ = _run(*(t.cuda() for t in (q, k, v)), mode)
+    ref = O.attention_flash(q, k, v).float().numpy()
+    assert rel_err(out.float().cpu().numpy(), ref) < 3e-3
+
+
 def test_split_and_unsplit_agree_within_tolerance():
     q, k, v = (t.cuda() for t in _inputs(8, 2048, seed=9))
     a, nb_split = _run(q, k, v, 0)
