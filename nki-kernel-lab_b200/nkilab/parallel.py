@@ -126,11 +126,11 @@ def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, variant: str = 
 def preferred_gather(world: int) -> str:
     """How the head-sharded attention's output should reach every rank: "nvlink" (the
     attention kernels store each output tile into every rank's buffer, PeerAttention) or
-    "nccl" (an all-gather after the kernels). Measured on B200s with 8 heads x 2048 x 128:
-    two GPUs 31.4 us per step over NVLink against 43.4 us with NCCL; eight GPUs 48.1 us
-    against 44.2 us (with one head per rank most output tiles come from the split-KV
-    combine kernel, whose stores to seven peers dominate)."""
-    return "nvlink" if world <= 2 else "nccl"
+    "nccl" (an all-gather after the kernels). Measured on B200s with 8 heads x 2048 x 128,
+    per step over NVLink against NCCL: two GPUs 31.4 against 43.4 us, four 37.9 against
+    41.9 us, eight 48.1 against 44.2 us (with one head per rank most output tiles come from
+    the split-KV combine kernel, whose stores to seven peers dominate)."""
+    return "nvlink" if world <= 4 else "nccl"
 
 
 class _RawCuda:
