@@ -75,6 +75,46 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed fp32 pairs (lo, hi) for fma.rn.f32x2 / add.rn.f32x2: each lane is an ordinary fp32
+// FMA / add, so the values equal those of the scalar forms, with half the instructions.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 f2_pack(float lo, float hi) {
+  return ((f32x2)__float_as_uint(hi) << 32) | __float_as_uint(lo);
+}
+__device__ __forceinline__ f32x2 f2_pack_bits(uint32_t lo, uint32_t hi) { return ((f32x2)hi << 32) | lo; }
+__device__ __forceinline__ float f2_lo(f32x2 a) { return __uint_as_float((uint32_t)a); }
+__device__ __forceinline__ float f2_hi(f32x2 a) { return __uint_as_float((uint32_t)(a >> 32)); }
+__device__ __forceinline__ f32x2 f2_fma(f32x2 a, f32x2 b, f32x2 c) {
+  f32x2 d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// P = 2^(s * scale_log2 - m) for the scores v[0..N), packed as bf16 pairs into v[0..N/2)
+// (pair (c, c+1) lands in v[c/2], a score already consumed). The row sum runs in `acc`
+// packed accumulators (acc = 1 or 2); accumulator j's lanes take the pairs with
+// (c/2) % acc == j, low lane the even scores, high lane the odd ones. Returns the
+// accumulators themselves so each caller combines them in its own order.
+template <int N, int ACC>
+__device__ __forceinline__ void exp_pack(uint32_t* v, float scale_log2, float neg_m, f32x2 (&rs)[ACC]) {
+  const f32x2 k2 = f2_pack(scale_log2, scale_log2), m2 = f2_pack(neg_m, neg_m);
+#pragma unroll
+  for (int j = 0; j < ACC; ++j) rs[j] = 0ull;
+#pragma unroll
+  for (int c = 0; c < N; c += 2) {
+    const f32x2 x2 = f2_fma(f2_pack_bits(v[c], v[c + 1]), k2, m2);
+    const float p0 = fast_exp2(f2_lo(x2)), p1 = fast_exp2(f2_hi(x2));
+    rs[(c >> 1) % ACC] = f2_add(rs[(c >> 1) % ACC], f2_pack(p0, p1));
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
+    v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
+  }
+}
+
 // Marks r[0..N) as defined here: placed after tcgen05.wait::ld, it keeps every use of
 // registers written by an asynchronous tcgen05.ld behind the wait that completes it.
 template <int N>
@@ -106,17 +146,9 @@ __device__ __forceinline__ float max64(const uint32_t* v) {
 // v[0..32) (pair (c, c+1) lands in v[c/2], a score already consumed); returns the fp32
 // sum of the 64 values.
 __device__ __forceinline__ float exp_pack64(uint32_t* v, float scale_log2, float neg_m) {
-  float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-  for (int c = 0; c < 64; c += 2) {
-    const float p0 = fast_exp2(fmaf(__uint_as_float(v[c]), scale_log2, neg_m));
-    const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + 1]), scale_log2, neg_m));
-    rs0 += p0;
-    rs1 += p1;
-    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-    v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
-  }
-  return rs0 + rs1;
+  f32x2 rs[1];
+  exp_pack<64, 1>(v, scale_log2, neg_m, rs);
+  return f2_lo(rs[0]) + f2_hi(rs[0]);
 }
 
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {

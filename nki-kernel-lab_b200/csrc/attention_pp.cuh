@@ -84,17 +84,9 @@ __device__ __forceinline__ bool lanes_wait(uint64_t* bar, uint32_t parity, volat
 // P = 2^(s * scale_log2 - m) for the 128 scores in v, packed as bf16 pairs into v[0..64)
 // (pair (c, c+1) lands in v[c/2], a score already consumed); returns the fp32 row sum.
 __device__ __forceinline__ float exp_pack128(uint32_t* v, float scale_log2, float neg_m) {
-  float rs[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-  for (int c = 0; c < 128; c += 2) {
-    const float p0 = fast_exp2(fmaf(__uint_as_float(v[c]), scale_log2, neg_m));
-    const float p1 = fast_exp2(fmaf(__uint_as_float(v[c + 1]), scale_log2, neg_m));
-    rs[(c >> 1) & 1] += p0;
-    rs[2 + ((c >> 1) & 1)] += p1;
-    __nv_bfloat162 h2 = __floats2bfloat162_rn(p0, p1);
-    v[c >> 1] = *reinterpret_cast<uint32_t*>(&h2);
-  }
-  return (rs[0] + rs[1]) + (rs[2] + rs[3]);
+  f32x2 rs[2];  // four fp32 chains: (even pairs, odd pairs) x (even scores, odd scores)
+  exp_pack<128, 2>(v, scale_log2, neg_m, rs);
+  return (f2_lo(rs[0]) + f2_lo(rs[1])) + (f2_hi(rs[0]) + f2_hi(rs[1]));
 }
 
 // Drain helper for the producers' abort path: wait (bounded) for an armed load to land.
