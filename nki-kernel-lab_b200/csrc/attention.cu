@@ -177,7 +177,6 @@ struct AttnSmem {
   uint64_t pv_step;    // one phase per P.V tile
   uint64_t pv_done;    // one phase per unit: its last P.V complete
   uint64_t o_free;     // engine has read O (all engine threads)
-  uint64_t qt_full[2];  // Q of the unit copied into TMEM buffer u & 1 (all engine threads)
   uint64_t mma_done;
   float xmax[2][2 * kTile];  // [tile parity][half * 128 + row]: row-max exchange
   float xsum[2 * kTile];     // [half * 128 + row]: row-sum exchange
@@ -412,7 +411,6 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       mbar_init(&s.v_empty[i], 1);
       mbar_init(&s.s_full[i], 1);
       mbar_init(&s.p_full[i], kEngineThreads);
-      mbar_init(&s.qt_full[i], kEngineThreads);
     }
     mbar_init(&s.pv_step, 1);
     mbar_init(&s.pv_done, 1);
@@ -482,8 +480,20 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
       for (int i = 0; ok && next_unit(args, i, un); ++i) {
         const int n = un.n;
         const int qb = qc & 1;
-        // the engine has copied the unit's Q from shared memory into TMEM buffer qb
-        if (!mbar_wait(&s.qt_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
+        // The unit's Q into TMEM buffer qb as the A operand of Q K^T (row r in lane r, bf16
+        // pairs (2j, 2j+1) in column j): one 128 x 32-byte copy per 16-column K step, from
+        // the same swizzled slices an SS-form MMA would read. The S MMAs below follow the
+        // copies in issue order. Buffer qb was last read by the S MMAs of the unit before
+        // the previous one, all complete (their scores have been consumed).
+        if (!mbar_wait(&s.q_full[qb], (qc >> 1) & 1u, &s.abort, &g_attn_dev_error, 20)) { ok = false; break; }
+        tc_fence_after();
+        {
+          const uint64_t q_desc = smem_desc_sw128(smem_u32(s.q[qb]), 16, 1024);
+          const uint32_t qt = tmem + kQtCol0 + (uint32_t)(qb * (D / 2));
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk)
+            tmem_cp_128x256b(qt + (uint32_t)(kk * 8), q_desc + (uint32_t)(((kk >> 2) * (kTile * 128) + (kk & 3) * 32) >> 4));
+        }
         ++qc;
         for (int t = 0; t < n && t < 2; ++t) {  // S for the unit's first two key tiles
           const uint32_t ki = kc + (uint32_t)t;
@@ -550,38 +560,7 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
     bool stored_any = false;
     uint32_t gt = 0, uc = 0;
     bool ok = true;
-    // Q of the unit with count c: from its shared-memory buffer c & 1 (128-byte-swizzled
-    // rows) into TMEM buffer c & 1 as the A operand of Q K^T (row r in lane r, bf16 pairs
-    // (2j, 2j+1) in column j); this warp copies its lane quadrant's rows, half hf of the
-    // columns.
-    auto copy_q = [&](uint32_t c) -> bool {
-      const int qb = c & 1;
-      if (!warp_wait(&s.q_full[qb], (c >> 1) & 1u, &s.abort, 30)) return false;
-      constexpr int kChunks = D / 16;  // 16-byte chunks of the row per warp half
-      uint32_t w[kChunks * 4];
-#pragma unroll
-      for (int j2 = 0; j2 < kChunks; ++j2) {
-        const int j = hf * kChunks + j2;  // chunk of the row: sub-tile j / 8, chunk j % 8
-        const uint4 x = *reinterpret_cast<const uint4*>(s.q[qb] + (j / 8) * (kTile * 128) + r * 128 +
-                                                         (((j & 7) ^ sw) * 16));
-        w[4 * j2] = x.x;
-        w[4 * j2 + 1] = x.y;
-        w[4 * j2 + 2] = x.z;
-        w[4 * j2 + 3] = x.w;
-      }
-      const uint32_t dst = tmem + lane_off + kQtCol0 + (uint32_t)(qb * (D / 2) + hf * (D / 4));
-      if constexpr (D == 128) {
-        tmem_st32(dst, w);
-      } else {
-        tmem_st16(dst, *reinterpret_cast<const uint32_t(*)[16]>(w));
-      }
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(&s.qt_full[qb]);
-      return true;
-    };
     UnitRun un;
-    if (next_unit(args, 0, un)) ok = copy_q(0);
     for (int i = 0; ok && next_unit(args, i, un); ++i) {
       const int u = un.u;
       const int qt = un.qt;
@@ -644,12 +623,6 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
         l = l * factor + rs;
       }
       if (!ok) break;
-      // the next unit's Q into the other TMEM buffer, so its first scores are computed
-      // while this unit's epilogue runs
-      {
-        UnitRun nx;
-        if (next_unit(args, i + 1, nx) && !copy_q(uc + 1)) { ok = false; break; }
-      }
       // ---------------- epilogue: O (complete after the unit's last P.V) -> output or partial
       if (!warp_wait(&s.pv_done, uc & 1u, &s.abort, 33)) { ok = false; break; }
       tc_fence_after();

@@ -214,6 +214,14 @@ __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Copy a 128-row x 32-byte slice of a shared-memory matrix (described by `s_desc`, as an
+// MMA operand would be) into TMEM: row i -> lane i, its 32 bytes -> 8 consecutive columns
+// from `taddr`. Asynchronous; an MMA issued after it by the same thread reads the copied
+// columns without further synchronisation (the pair is pipelined in issue order).
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(s_desc) : "memory");
+}
+
 // Arrive on an mbarrier once every tcgen05 op issued so far by this thread completes.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
