@@ -97,8 +97,7 @@ def test_matmul_bf16_property_any_shape(M, K, N):
 @pytest.mark.parametrize("M,K,N", [(128, 64, 128), (129, 72, 264), (1, 8, 8), (300, 1000, 520), (1024, 1024, 1024),
                                    (2048, 512, 4096), (4000, 1000, 3000)])
 def test_matmul_bf16_tiles(ops, M, K, N):
-    """Single-CTA tiles (up to 1024^3) and, from 2048 x 512 x 4096 on, the CTA-pair kernel's
-    256 x 256 tiles, the last case with partial tiles in M, N and K."""
+    """Every tile width (64, 128, 256 columns), the last case with partial tiles in M, N and K."""
     g = torch.Generator().manual_seed(M + K + N)
     a = (torch.rand(M, K, generator=g) * 2 - 1).to(torch.bfloat16)
     b = (torch.rand(K, N, generator=g) * 2 - 1).to(torch.bfloat16)
