@@ -94,6 +94,11 @@ __device__ __forceinline__ f32x2 f2_add(f32x2 a, f32x2 b) {
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ f32x2 f2_mul(f32x2 a, f32x2 b) {
+  f32x2 d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 // P = 2^(s * scale_log2 - m) for the scores v[0..N), packed as bf16 pairs into v[0..N/2)
 // (pair (c, c+1) lands in v[c/2], a score already consumed). The row sum runs in `acc`
@@ -613,7 +618,11 @@ attn_fwd_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_con
           tmem_wait_ld();
           reg_fence<D / 2>(v);
 #pragma unroll
-          for (int k2 = 0; k2 < D / 2; ++k2) v[k2] = __float_as_uint(__uint_as_float(v[k2]) * factor);
+          for (int k2 = 0; k2 < D / 2; k2 += 2) {  // O *= factor, two columns per mul.rn.f32x2
+            const f32x2 o2 = f2_mul(f2_pack_bits(v[k2], v[k2 + 1]), f2_pack(factor, factor));
+            v[k2] = (uint32_t)o2;
+            v[k2 + 1] = (uint32_t)(o2 >> 32);
+          }
 #pragma unroll
           for (int c = 0; c < D / 64; ++c) tmem_st32(o_addr + c * 32, v + c * 32);
         }

@@ -422,7 +422,11 @@ attn_fwd_pp_bf16_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_
             tmem_wait_ld();
             reg_fence<64>(v + 64);
 #pragma unroll
-            for (int k2 = 64; k2 < 128; ++k2) v[k2] = __float_as_uint(__uint_as_float(v[k2]) * factor);
+            for (int k2 = 64; k2 < 128; k2 += 2) {  // two columns per mul.rn.f32x2
+              const f32x2 o2 = f2_mul(f2_pack_bits(v[k2], v[k2 + 1]), f2_pack(factor, factor));
+              v[k2] = (uint32_t)o2;
+              v[k2 + 1] = (uint32_t)(o2 >> 32);
+            }
             tmem_st32(o_own + c * 64, v + 64);
             tmem_st32(o_own + c * 64 + 32, v + 96);
             tmem_wait_st();  // before the registers take the next columns
