@@ -374,7 +374,7 @@ def bench_gemm(dev, stream, pk) -> dict:
         tf = 2.0 * n ** 3 / (ms * 1e-3) / 1e12
         out[f"{n}^3"] = {"us": round(ms * 1e3, 2), "tflops": round(tf, 1), "frac": round(tf / pk["bf16_tflops"], 4),
                          "cublas_us_same_run": round(ms_cublas * 1e3, 2),
-                         "traffic_bytes_per_launch": ncu_traffic("gemm_bf16_tc_1024_8192.md", str(n))}
+                         "traffic_bytes_per_launch": ncu_traffic("gemm_bf16_1024_8192.md", str(n))}
         del sets
     return out
 
