@@ -105,6 +105,37 @@ def test_matmul_bf16_tiles(ops, M, K, N):
     check_bf16(to_numpy(out), to_numpy(O.matmul(a, b)))
 
 
+@pytest.mark.parametrize("M,K,N", [(4096, 4096, 4096), (4000, 1000, 3000)])
+def test_matmul_cta_pairs_replayed_from_a_graph_on_a_side_stream(ops, M, K, N):
+    """Large GEMMs run on the CTA-pair kernel (clusters of two CTAs). Captured into a CUDA
+    graph on a non-default stream, where programmatic dependent launch takes effect between
+    consecutive launches, the replays must give the eager results bit for bit and leave no
+    device-side error (a launch that lost its cluster shape would report one)."""
+    from nkilab import _native as N_
+
+    g = torch.Generator(device="cuda").manual_seed(M + N)
+    a = (torch.rand(M, K, device="cuda", generator=g) * 2 - 1).to(torch.bfloat16)
+    b = (torch.rand(K, N, device="cuda", generator=g) * 2 - 1).to(torch.bfloat16)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        eager = [torch.ops.nkilab.matmul(a, b, False) for _ in range(3)]
+    torch.cuda.synchronize()
+    N_.check_device(s.cuda_stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            replayed = [torch.ops.nkilab.matmul(a, b, False) for _ in range(3)]
+    for _ in range(2):
+        with torch.cuda.stream(s):
+            graph.replay()
+        torch.cuda.synchronize()
+        N_.check_device(s.cuda_stream)
+        assert all(torch.equal(r, eager[0]) for r in replayed)
+    assert all(torch.equal(e, eager[0]) for e in eager)
+    check_bf16(to_numpy(eager[0][:256].cpu()), to_numpy(O.matmul(a[:256].cpu(), b.cpu())))
+    del graph
+
+
 def test_matmul_8192_cube_sampled_rows(ops):
     """BASELINE's large config: full product on the GPU, 96 random rows checked on the CPU."""
     g = torch.Generator().manual_seed(8192)
