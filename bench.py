@@ -450,7 +450,7 @@ def bench_block(dev, stream, pk, ctx) -> dict:
         ctx["barrier"]()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
-        steps = 3
+        steps = 10  # ~50 ms per variant; 3 steps left the variants' order to noise at two GPUs
         t0.record(stream)
         for _ in range(steps):
             fwd()
