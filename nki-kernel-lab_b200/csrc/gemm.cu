@@ -15,6 +15,9 @@
 //   warps 2-5   epilogue: tcgen05.ld the fp32 accumulator (thread = output row),
 //               round to bf16, store; two TMEM accumulators so the epilogue of tile
 //               i overlaps the main loop of tile i+1
+// Large bf16 GEMMs take gemm_bf16_pair_kernel instead: the same roles in clusters of two
+// CTAs that share M = 256 MMAs (tcgen05 cta_group::2) on 256 x 256 tiles, halving each
+// CTA's share of the B tile it loads (see the comment above that kernel).
 // fp32 path: exact fp32 FMA tiled kernel on CUDA cores (tcgen05 has no full-precision
 // fp32 MMA; kind::tf32 would miss the reference's 1e-5 fp32 tolerance).
 #include <atomic>
