@@ -159,32 +159,6 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
   return NKL_OK;
 }
 
-// As launch_pdl, for a kernel launched as clusters of `cluster_x` CTAs along x.
-template <typename... KArgs, typename... Args>
-int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, unsigned cluster_x, size_t smem,
-                       cudaStream_t st, const char* what, Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = cluster_x;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
-  if (e != cudaSuccess) {
-    (void)cudaGetLastError();
-    return fail(NKL_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-  }
-  return NKL_OK;
-}
-
 // exp(x) for the row kernels: the accurate library expf for fp32 outputs (the
 // reference's fp32 tolerances are 1e-5), the fast hardware-approximate __expf when
 // the result is rounded to bf16 (its error is far below one bf16 ulp).

@@ -15,9 +15,6 @@
 //   warps 2-5   epilogue: tcgen05.ld the fp32 accumulator (thread = output row),
 //               round to bf16, store; two TMEM accumulators so the epilogue of tile
 //               i overlaps the main loop of tile i+1
-// Large bf16 GEMMs take gemm_bf16_pair_kernel instead: the same roles in clusters of two
-// CTAs that share M = 256 MMAs (tcgen05 cta_group::2) on 256 x 256 tiles, halving each
-// CTA's share of the B tile it loads (see the comment above that kernel).
 // fp32 path: exact fp32 FMA tiled kernel on CUDA cores (tcgen05 has no full-precision
 // fp32 MMA; kind::tf32 would miss the reference's 1e-5 fp32 tolerance).
 #include <atomic>
@@ -75,89 +72,6 @@ __device__ __forceinline__ void tile_coords(int t, int m_tiles, int n_tiles, int
 // across GPUs before their one rounding).
 constexpr int kEpiStore = 0, kEpiSwiglu = 1, kEpiResidual = 2, kEpiF32 = 3;
 
-// Epilogue of one output tile for the 128 rows of a CTA: the thread of TMEM lane `row`
-// reads its row of the fp32 accumulator (columns from `acc_addr`, which carries the lane
-// quadrant) and writes output row gm of column tile nt, per EPI.
-template <int BN, int EPI>
-__device__ __forceinline__ void gemm_store_rows(uint32_t acc_addr, int gm, int nt, void* c_out,
-                                                const bf16* __restrict__ res, int M, int N) {
-  bf16* const c = static_cast<bf16*>(c_out);
-  if constexpr (EPI == kEpiSwiglu) {
-    static_assert(BN == 256, "the fused SwiGLU epilogue pairs 128 gate with 128 up columns");
-    const int F = N / 2;
-    bf16* orow = c + (int64_t)gm * F;
-#pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
-      uint32_t rg[32], ru[32];
-      const uint32_t base = acc_addr + (uint32_t)(cc * 32);
-      tmem_ld32(base, rg);
-      tmem_ld32(base + 128, ru);
-      tmem_wait_ld();
-      const int gn = nt * 128 + cc * 32;
-      if (gm < M) {
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          if (gn + v * 8 < F) {
-            float f[8];
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[v * 8 + e])));
-              const float u = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[v * 8 + e])));
-              f[e] = silu_f32<bf16>(g) * u;
-            }
-            *reinterpret_cast<uint4*>(orow + gn + v * 8) = pack16<bf16>(f);
-          }
-        }
-      }
-    }
-    return;
-  }
-  if constexpr (EPI == kEpiF32) {
-    float* frow = static_cast<float*>(c_out) + (int64_t)gm * N;
-#pragma unroll 1
-    for (int cc = 0; cc < BN / 32; ++cc) {
-      uint32_t r[32];
-      tmem_ld32(acc_addr + (uint32_t)(cc * 32), r);
-      tmem_wait_ld();
-      const int gn = nt * BN + cc * 32;
-      if (gm < M) {
-#pragma unroll
-        for (int v = 0; v < 8; ++v)  // N % 8 == 0: a 4-column group is all in range or all out
-          if (gn + v * 4 < N)
-            *reinterpret_cast<uint4*>(frow + gn + v * 4) =
-                make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-      }
-    }
-    return;
-  }
-  bf16* crow = c + (int64_t)gm * N;
-  const bf16* rrow = EPI == kEpiResidual ? res + (int64_t)gm * N : nullptr;
-#pragma unroll 1
-  for (int cc = 0; cc < BN / 32; ++cc) {
-    uint32_t r[32];
-    tmem_ld32(acc_addr + (uint32_t)(cc * 32), r);
-    tmem_wait_ld();
-    const int gn = nt * BN + cc * 32;
-    if (gm < M) {
-#pragma unroll
-      for (int v = 0; v < 4; ++v) {
-        if (gn + v * 8 < N) {
-          float f[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
-          if constexpr (EPI == kEpiResidual) {
-            Vec16<bf16> rv;
-            rv.raw = *reinterpret_cast<const uint4*>(rrow + gn + v * 8);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(__float2bfloat16_rn(f[e])) + rv.get(e);
-          }
-          *reinterpret_cast<uint4*>(crow + gn + v * 8) = pack16<bf16>(f);
-        }
-      }
-    }
-  }
-}
-
 template <int BN, int STAGES, int EPI = kEpiStore>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
@@ -175,6 +89,7 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   const int lane = threadIdx.x & 31;
   const int num_tiles = m_tiles * n_tiles;
   const int k_blocks = (K + kBK - 1) / kBK;
+  bf16* const c = static_cast<bf16*>(c_out);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) {
@@ -299,8 +214,85 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
       ok = __shfl_sync(0xffffffffu, ok, 0);  // whole warp follows lane 0 (keeps .sync.aligned ops converged)
       if (!ok) break;
       tc_fence_after();
-      gemm_store_rows<BN, EPI>(tmem + (uint32_t)(acc * BN) + ((uint32_t)(q * 32) << 16), mt * kBM + row, nt, c_out,
-                               res, M, N);
+      const int gm = mt * kBM + row;
+      if constexpr (EPI == kEpiSwiglu) {
+        static_assert(BN == 256, "the fused SwiGLU epilogue pairs 128 gate with 128 up columns");
+        const int F = N / 2;
+        bf16* orow = c + (int64_t)gm * F;
+#pragma unroll 1
+        for (int cc = 0; cc < 4; ++cc) {
+          uint32_t rg[32], ru[32];
+          const uint32_t base = tmem + (uint32_t)(acc * BN + cc * 32) + ((uint32_t)(q * 32) << 16);
+          tmem_ld32(base, rg);
+          tmem_ld32(base + 128, ru);
+          tmem_wait_ld();
+          const int gn = nt * 128 + cc * 32;
+          if (gm < M) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              if (gn + v * 8 < F) {
+                float f[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float g = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rg[v * 8 + e])));
+                  const float u = __bfloat162float(__float2bfloat16_rn(__uint_as_float(ru[v * 8 + e])));
+                  f[e] = silu_f32<bf16>(g) * u;
+                }
+                *reinterpret_cast<uint4*>(orow + gn + v * 8) = pack16<bf16>(f);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s.acc_empty[acc]);
+        continue;
+      }
+      if constexpr (EPI == kEpiF32) {
+        float* frow = static_cast<float*>(c_out) + (int64_t)gm * N;
+#pragma unroll 1
+        for (int cc = 0; cc < BN / 32; ++cc) {
+          uint32_t r[32];
+          tmem_ld32(tmem + (uint32_t)(acc * BN + cc * 32) + ((uint32_t)(q * 32) << 16), r);
+          tmem_wait_ld();
+          const int gn = nt * BN + cc * 32;
+          if (gm < M) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)  // N % 8 == 0: a 4-column group is all in range or all out
+              if (gn + v * 4 < N)
+                *reinterpret_cast<uint4*>(frow + gn + v * 4) =
+                    make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(&s.acc_empty[acc]);
+        continue;
+      }
+      bf16* crow = c + (int64_t)gm * N;
+      const bf16* rrow = EPI == kEpiResidual ? res + (int64_t)gm * N : nullptr;
+#pragma unroll 1
+      for (int cc = 0; cc < BN / 32; ++cc) {
+        uint32_t r[32];
+        tmem_ld32(tmem + (uint32_t)(acc * BN + cc * 32) + ((uint32_t)(q * 32) << 16), r);
+        tmem_wait_ld();
+        const int gn = nt * BN + cc * 32;
+        if (gm < M) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            if (gn + v * 8 < N) {
+              float f[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = __uint_as_float(r[v * 8 + e]);
+              if constexpr (EPI == kEpiResidual) {
+                Vec16<bf16> rv;
+                rv.raw = *reinterpret_cast<const uint4*>(rrow + gn + v * 8);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) f[e] = __bfloat162float(__float2bfloat16_rn(f[e])) + rv.get(e);
+              }
+              *reinterpret_cast<uint4*>(crow + gn + v * 8) = pack16<bf16>(f);
+            }
+          }
+        }
+      }
       tc_fence_before();
       mbar_arrive(&s.acc_empty[acc]);
     }
@@ -310,223 +302,6 @@ gemm_bf16_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_cons
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
-  }
-}
-
-// ------------------------------------------------------------------ CTA-pair bf16 path
-// Large GEMMs: a cluster of two CTAs computes a 256 x 256 output tile with M = 256 MMAs
-// (tcgen05 cta_group::2) issued by CTA 0. Each CTA loads its 128 rows of A and its 128
-// columns of B per k-block (no multicast: every byte it loads lands in its own shared
-// memory), so a CTA moves 32 KB from L2 per k-block for a 128 x 256 share of the output
-// where the single-CTA 128 x 256 tile moves 48 KB. At 148 SMs the single-CTA kernel needs
-// about 25 TB/s from L2 to keep the tensor pipe busy, above what L2 delivers; the pair
-// needs about 17. Each CTA keeps its 128 rows of both accumulators in its own TMEM and runs
-// the same epilogue as the single-CTA kernel.
-constexpr int kPairBM = 256, kPairBN = 256, kPairStages = 6;
-
-struct PairSmem {
-  uint8_t a[kPairStages][kBM * kBK * 2];              // this CTA's 128 rows of the A k-block (16 KB)
-  uint8_t b[kPairStages][kBK * (kPairBN / 2) * 2];    // its 128 columns of the B k-block: 2 boxes of [64 x 128 B]
-  uint64_t full[kPairStages];   // CTA 0: both CTAs' loads of the stage have landed
-  uint64_t empty[kPairStages];  // each CTA: the MMAs reading the stage have completed
-  uint64_t acc_full[2];         // each CTA: the accumulator's MMAs have completed
-  uint64_t acc_empty[2];        // CTA 0: both CTAs' epilogues have read the accumulator (256 arrivals)
-  uint64_t mma_done;            // CTA 0
-  uint32_t tmem_base;
-  int abort;
-};
-
-constexpr size_t pair_smem_bytes() { return sizeof(PairSmem) + 1024; }
-static_assert(pair_smem_bytes() <= 232448, "CTA-pair GEMM shared memory above the 227 KB per-block limit");
-
-template <int EPI>
-__global__ void __launch_bounds__(kGemmThreads, 1)
-gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                      void* __restrict__ c_out, const bf16* __restrict__ res, int M, int N, int K, int m_tiles,
-                      int n_tiles) {
-  extern __shared__ uint8_t smem_raw[];
-  {
-    // Launched as clusters of two (the launch attribute set by launch_pair). Otherwise no
-    // CTA has a peer: report it and return before any barrier, TMEM or memory access.
-    uint32_t ncta;
-    asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(ncta));
-    if (ncta != 2) {
-      if (threadIdx.x == 0) atomicCAS(&g_gemm_dev_error, 0u, 15u);
-      return;
-    }
-  }
-  pdl_launch_dependents();
-  // The same 1024-aligned offset in both CTAs: the MMA addresses the peer's operands at the
-  // offsets of CTA 0's.
-  auto& s = *reinterpret_cast<PairSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  constexpr uint32_t kTmemCols = 2 * kPairBN;
-  constexpr uint32_t kIdesc = idesc_bf16_f32(kPairBM, kPairBN, false, true);
-  constexpr uint32_t kStageBytes = (kBM * kBK + kBK * (kPairBN / 2)) * 2;  // per CTA
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
-  const int pair = (int)(blockIdx.x >> 1), pairs = (int)(gridDim.x >> 1);
-  const int num_tiles = m_tiles * n_tiles;
-  const int k_blocks = (K + kBK - 1) / kBK;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kPairStages; ++i) {
-      mbar_init(&s.full[i], 1);
-      mbar_init(&s.empty[i], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s.acc_full[i], 1);
-      mbar_init(&s.acc_empty[i], 256);
-    }
-    mbar_init(&s.mma_done, 1);
-    s.abort = 0;
-    fence_barrier_init();
-  }
-  if (warp == 0 && lane == 0) {
-    tma_prefetch_desc(&map_a);
-    tma_prefetch_desc(&map_b);
-  }
-  if (warp == 1) tmem_alloc_pair(&s.tmem_base, kTmemCols);
-  tc_fence_before();
-  cluster_sync();  // both CTAs' barriers are initialised and their TMEM allocated
-  tc_fence_after();
-  const uint32_t tmem = s.tmem_base;
-  // Programmatic dependent launch, as the single-CTA kernel: the first tile's first
-  // k-blocks are prefetched into L2 before the wait.
-  if (warp == 0 && elect_one() && pair < num_tiles) {
-    int mt, nt;
-    tile_coords(pair, m_tiles, n_tiles, mt, nt);
-    const int pre = k_blocks < kPairStages ? k_blocks : kPairStages;
-    for (int kb = 0; kb < pre; ++kb) {
-      tma_prefetch_2d(&map_a, kb * kBK, mt * kPairBM + (int)rank * kBM);
-#pragma unroll
-      for (int j = 0; j < 2; ++j) tma_prefetch_2d(&map_b, nt * kPairBN + (int)rank * 128 + j * 64, kb * kBK);
-    }
-  }
-  __syncwarp();
-  pdl_wait();
-
-  if (warp == 0) {
-    // ---------------- TMA producer (both CTAs); completions are counted on CTA 0's full[]
-    if (elect_one()) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int armed_phase[kPairStages];
-#pragma unroll
-      for (int i = 0; i < kPairStages; ++i) armed_phase[i] = -1;
-      bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += pairs) {
-        int mt, nt;
-        tile_coords(t, m_tiles, n_tiles, mt, nt);
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&s.empty[stage], phase ^ 1u, &s.abort, &g_gemm_dev_error, 11)) { ok = false; break; }
-          if (rank == 0) {
-            mbar_arrive_expect_tx(&s.full[stage], 2 * kStageBytes);  // both CTAs' bytes
-            armed_phase[stage] = (int)phase;
-          }
-          const uint32_t full0 = cluster_addr(&s.full[stage], 0);
-          tma_load_2d_pair(s.a[stage], &map_a, full0, kb * kBK, mt * kPairBM + (int)rank * kBM);
-#pragma unroll
-          for (int j = 0; j < 2; ++j)
-            tma_load_2d_pair(s.b[stage] + j * (kBK * 128), &map_b, full0, nt * kPairBN + (int)rank * 128 + j * 64,
-                             kb * kBK);
-          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
-        }
-      }
-      if (!ok && rank == 0) {
-        // Let copies already issued land (CTA 0's full[] counts both CTAs' bytes) before
-        // the pair's shared memory is released; the final cluster barrier holds CTA 1.
-        for (int i = 0; i < kPairStages; ++i) {
-          if (armed_phase[i] < 0) continue;
-          const uint64_t t0 = globaltimer();
-          while (!mbar_try_wait(&s.full[i], (uint32_t)armed_phase[i]) && globaltimer() - t0 < kWaitTimeoutNs) {}
-        }
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer (CTA 0 only)
-    if (rank == 0 && elect_one()) {
-      int stage = 0;
-      uint32_t phase = 0;
-      int it = 0;
-      bool ok = true;
-      for (int t = pair; t < num_tiles && ok; t += pairs, ++it) {
-        const int acc = it & 1;
-        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-        {  // both CTAs' epilogues have read this accumulator (arrivals from CTA 1 are remote)
-          const uint32_t par = acc_phase ^ 1u;
-          if (!mbar_try_wait_cluster(&s.acc_empty[acc], par)) {
-            const uint64_t t0 = globaltimer();
-            while (!mbar_try_wait_cluster(&s.acc_empty[acc], par)) {
-              volatile int* ab = &s.abort;
-              if (*ab || globaltimer() - t0 > kWaitTimeoutNs) {
-                *ab = 1;
-                atomicCAS(&g_gemm_dev_error, 0u, 12u);
-                ok = false;
-                break;
-              }
-            }
-            if (!ok) break;
-          }
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + (uint32_t)(acc * kPairBN);
-        for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait(&s.full[stage], phase, &s.abort, &g_gemm_dev_error, 13)) { ok = false; break; }
-          tc_fence_after();
-          const uint32_t a_base = smem_u32(s.a[stage]);
-          const uint32_t b_base = smem_u32(s.b[stage]);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint64_t ad = smem_desc_sw128(a_base + kk * 32, 16, 1024);
-            const uint64_t bd = smem_desc_sw128(b_base + kk * 2048, kBK * 128, 1024);
-            mma_bf16_ss_pair(d_tmem, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
-          }
-          mma_commit_pair(&s.empty[stage], 0x3);  // frees the stage in both CTAs
-          if (++stage == kPairStages) { stage = 0; phase ^= 1u; }
-        }
-        if (ok) mma_commit_pair(&s.acc_full[acc], 0x3);
-      }
-      // Every MMA issued by this thread has completed once mma_done flips.
-      mma_commit_pair(&s.mma_done, 0x1);
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(&s.mma_done, 0) && globaltimer() - t0 < kWaitTimeoutNs) {}
-    }
-    __syncwarp();
-  } else {
-    // ---------------- epilogue (warps 2..5 = TMEM lane quadrants 2,3,0,1), both CTAs
-    const int q = warp & 3;
-    const int row = q * 32 + lane;
-    const uint32_t acc_empty0[2] = {cluster_addr(&s.acc_empty[0], 0), cluster_addr(&s.acc_empty[1], 0)};
-    int it = 0;
-    for (int t = pair; t < num_tiles; t += pairs, ++it) {
-      int mt, nt;
-      tile_coords(t, m_tiles, n_tiles, mt, nt);
-      const int acc = it & 1;
-      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-      int ok = 1;
-      if (lane == 0) ok = mbar_wait(&s.acc_full[acc], acc_phase, &s.abort, &g_gemm_dev_error, 14) ? 1 : 0;
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) break;
-      tc_fence_after();
-      gemm_store_rows<kPairBN, EPI>(tmem + (uint32_t)(acc * kPairBN) + ((uint32_t)(q * 32) << 16),
-                                    mt * kPairBM + (int)rank * kBM + row, nt, c_out, res, M, N);
-      tc_fence_before();
-      if (rank == 0) mbar_arrive(&s.acc_empty[acc]);
-      else mbar_arrive_cluster(acc_empty0[acc]);
-    }
-  }
-
-  // Neither CTA releases its shared memory or TMEM while the pair's MMAs or the other CTA
-  // may still use them.
-  tc_fence_before();
-  __syncthreads();
-  cluster_sync();
-  if (warp == 1) {
-    tc_fence_after();
-    tmem_dealloc_pair(tmem, kTmemCols);
   }
 }
 
@@ -630,72 +405,6 @@ int launch_tc(const void* a, const void* b, void* c, int M, int N, int K, cudaSt
                     mb, c, static_cast<const bf16*>(res), M, N, K, m_tiles, n_tiles);
 }
 
-// Most CTA pairs of gemm_bf16_pair_kernel resident at once on this device (a pair needs
-// two SMs of one GPC), from the occupancy API, cached per device.
-template <int EPI>
-int pair_slots() {
-  static std::atomic<int> cached[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev >= 0 && dev < 64) {
-    const int v = cached[dev].load(std::memory_order_acquire);
-    if (v != 0) return v;
-  }
-  constexpr size_t smem = pair_smem_bytes();
-  cudaError_t e =
-      cudaFuncSetAttribute(gemm_bf16_pair_kernel<EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  int n = 0;
-  if (e == cudaSuccess) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2);
-    cfg.blockDim = dim3(kGemmThreads);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaOccupancyMaxActiveClusters(&n, gemm_bf16_pair_kernel<EPI>, &cfg);
-  }
-  if (e != cudaSuccess || n <= 0) {
-    (void)cudaGetLastError();
-    n = -1;  // the pair kernel is not used on this device
-  }
-  if (dev >= 0 && dev < 64) cached[dev].store(n, std::memory_order_release);
-  return n;
-}
-
-template <int EPI>
-int launch_pair(const void* a, const void* b, void* c, int M, int N, int K, int pairs, cudaStream_t st,
-                const void* res) {
-  CUtensorMap ma, mb;
-  {
-    const uint64_t dims[2] = {(uint64_t)K, (uint64_t)M};
-    const uint64_t strides[1] = {(uint64_t)K * 2};
-    const uint32_t box[2] = {kBK, kBM};
-    int rc = make_tensor_map_bf16(&ma, a, 2, dims, strides, box, "nkl_matmul(A)");
-    if (rc) return rc;
-  }
-  {
-    const uint64_t dims[2] = {(uint64_t)N, (uint64_t)K};
-    const uint64_t strides[1] = {(uint64_t)N * 2};
-    const uint32_t box[2] = {64, kBK};
-    int rc = make_tensor_map_bf16(&mb, b, 2, dims, strides, box, "nkl_matmul(B)");
-    if (rc) return rc;
-  }
-  const int m_tiles = (M + kPairBM - 1) / kPairBM;
-  const int n_tiles = (N + kPairBN - 1) / kPairBN;
-  const int tiles = m_tiles * n_tiles;
-  const int grid_pairs = tiles < pairs ? tiles : pairs;
-  // The cluster shape is a launch attribute (recorded with the launch when it is captured
-  // into a CUDA graph), not a compile-time property of the kernel.
-  return launch_pdl_cluster(gemm_bf16_pair_kernel<EPI>, dim3(2 * grid_pairs), dim3(kGemmThreads), 2,
-                            pair_smem_bytes(), st, "nkl_matmul", ma, mb, c, static_cast<const bf16*>(res), M, N, K,
-                            m_tiles, n_tiles);
-}
-
 // Tile width by how many tiles the SMs get. 256-column tiles read 96 B/clk of MMA
 // operands from shared memory per SM and keep the tensor pipe fed; 128-column tiles need
 // 128 B/clk, at the limit, so they are used only when 256-column tiles would leave more
@@ -704,14 +413,6 @@ int launch_pair(const void* a, const void* b, void* c, int M, int N, int K, int 
 template <int EPI>
 int dispatch_tc(const void* a, const void* b, void* c, const void* res, int64_t M, int64_t N, int64_t K,
                 cudaStream_t st) {
-  // CTA pairs with 256 x 256 tiles once the tiles fill every pair slot at least twice
-  // (with fewer, the single-CTA tiles measured as fast or faster: 2048 x 512 x 4096)
-  const int64_t pair_tiles = ((M + kPairBM - 1) / kPairBM) * ((N + kPairBN - 1) / kPairBN);
-  if (pair_tiles >= sm_count()) {
-    int pairs = pair_slots<EPI>();
-    if (pairs > sm_count() / 2) pairs = sm_count() / 2;
-    if (pairs > 0) return launch_pair<EPI>(a, b, c, (int)M, (int)N, (int)K, pairs, st, res);
-  }
   const int64_t m_tiles = (M + kBM - 1) / kBM;
   const int64_t tiles256 = m_tiles * ((N + 255) / 256);
   const int64_t tiles128 = m_tiles * ((N + 127) / 128);

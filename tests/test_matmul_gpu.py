@@ -106,11 +106,10 @@ def test_matmul_bf16_tiles(ops, M, K, N):
 
 
 @pytest.mark.parametrize("M,K,N", [(4096, 4096, 4096), (4000, 1000, 3000)])
-def test_matmul_cta_pairs_replayed_from_a_graph_on_a_side_stream(ops, M, K, N):
-    """Large GEMMs run on the CTA-pair kernel (clusters of two CTAs). Captured into a CUDA
-    graph on a non-default stream, where programmatic dependent launch takes effect between
-    consecutive launches, the replays must give the eager results bit for bit and leave no
-    device-side error (a launch that lost its cluster shape would report one)."""
+def test_matmul_replayed_from_a_graph_on_a_side_stream(ops, M, K, N):
+    """Large GEMMs captured into a CUDA graph on a non-default stream, where programmatic
+    dependent launch takes effect between consecutive launches: the replays give the eager
+    results bit for bit and leave no device-side error."""
     from nkilab import _native as N_
 
     g = torch.Generator(device="cuda").manual_seed(M + N)
